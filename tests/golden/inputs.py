@@ -1,0 +1,78 @@
+"""Deterministic inputs shared by the golden generator and the tests.
+
+Every golden case is rebuilt from a numpy ``default_rng`` seed, so the
+fixtures only hold the reference's outputs.  ``make_golden.py`` feeds these
+exact arrays to the reference; the tests feed them to the oracle and to the
+CUDA path.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Dict
+
+import numpy as np
+
+# name: hidden, heads, dim_head, q_len, cache_len, rope grid, start_frame,
+#       gated, init, audio rope, new_kv_real_len, compute dtypes
+ATTN_CASES: Dict[str, dict] = {
+    # Config 1 (CPU fp32): hidden 256, 4 x 64, one 8x12 query frame, six cached frames.
+    "c1": dict(hidden=256, heads=4, dim_head=64, lq=96, lcache=576, grid=(1, 8, 12), start=6,
+               gated=False, init="xavier", audio=False, real_len=None, seed=0),
+    # Head dim 128 with ragged lengths (query 160, cache 300).
+    "d128": dict(hidden=512, heads=4, dim_head=128, lq=160, lcache=300, grid=(1, 10, 16), start=5,
+                 gated=False, init="normal", audio=False, real_len=None, seed=1),
+    # Per-head gated attention, empty cache (first block).
+    "gated": dict(hidden=256, heads=4, dim_head=64, lq=96, lcache=0, grid=(1, 8, 12), start=0,
+                  gated=True, init="normal", audio=False, real_len=None, seed=2),
+    # Audio-like: 28 padded query rows, real K/V length 25, 101 cached, 1-D audio RoPE.
+    "audio": dict(hidden=512, heads=8, dim_head=64, lq=28, lcache=101, grid=(28,), start=26,
+                  gated=False, init="normal", audio=True, real_len=25, seed=3),
+}
+
+
+def _xavier(rng, out_f, in_f):
+    a = math.sqrt(6.0 / (in_f + out_f))
+    return rng.uniform(-a, a, size=(out_f, in_f)).astype(np.float32)
+
+
+def attn_case_inputs(name: str) -> dict:
+    """Seeded inputs for one golden attention case (float32 arrays, batch 1
+    dropped).  Weights use torch's ``[out, in]`` layout."""
+    c = ATTN_CASES[name]
+    rng = np.random.default_rng(1000 + c["seed"])
+    hid, inner = c["hidden"], c["heads"] * c["dim_head"]
+    p = {}
+    for nm, (o, i) in {"to_q": (inner, hid), "to_k": (inner, hid), "to_v": (inner, hid),
+                       "to_out": (hid, inner)}.items():
+        if c["init"] == "xavier":
+            p[nm + "_w"] = _xavier(rng, o, i)
+            p[nm + "_b"] = np.zeros(o, np.float32)
+        else:
+            p[nm + "_w"] = (rng.standard_normal((o, i)) * 0.02).astype(np.float32)
+            p[nm + "_b"] = (rng.standard_normal(o) * 0.02).astype(np.float32)
+    if c["gated"]:
+        p["to_gate_logits_w"] = (rng.standard_normal((c["heads"], hid)) * 0.02).astype(np.float32)
+        p["to_gate_logits_b"] = (rng.standard_normal(c["heads"]) * 0.02).astype(np.float32)
+    p["q_norm_w"] = rng.uniform(0.5, 1.5, inner).astype(np.float32)
+    p["k_norm_w"] = rng.uniform(0.5, 1.5, inner).astype(np.float32)
+    x = rng.standard_normal((c["lq"], hid)).astype(np.float32)
+    ck = cv = None
+    if c["lcache"]:
+        ck = rng.standard_normal((c["lcache"], c["heads"], c["dim_head"])).astype(np.float32)
+        cv = rng.standard_normal((c["lcache"], c["heads"], c["dim_head"])).astype(np.float32)
+    return dict(cfg=c, params=p, x=x, cached_k=ck, cached_v=cv)
+
+
+def split_rope_inputs() -> np.ndarray:
+    """x ``[96, 256]`` for the split-RoPE case (C1 shapes)."""
+    return np.random.default_rng(77).standard_normal((96, 256)).astype(np.float32)
+
+
+def a2a_inputs():
+    """Full (unsharded) tensors for the all-to-all cases."""
+    rng = np.random.default_rng(1234)
+    full = rng.standard_normal((1, 24, 8, 4)).astype(np.float32)
+    full2 = rng.standard_normal((1, 24, 8, 4)).astype(np.float32)
+    raw = rng.standard_normal((1, 25, 6)).astype(np.float32)
+    return full, full2, raw
