@@ -1,0 +1,175 @@
+/*
+ * taomate_b200: C ABI of the B200 (sm_100a) kernels for TaoMate's causal-LTX
+ * streaming attention step.
+ *
+ * All pointers are device pointers owned by the caller (PyTorch's caching
+ * allocator in the Python host layer); the library never frees them and never
+ * keeps them past the call.  `stream` is a cudaStream_t passed as void*; all
+ * work is stream-ordered and no entry point synchronises the host, except
+ * tm_device_error().  Every entry point returns a tm_status; on error
+ * tm_last_error() gives a one-line message (thread-local).
+ *
+ * Reference paths below are relative to the TaoLiveAIGC/TaoMate source tree.
+ */
+#ifndef TAOMATE_B200_H
+#define TAOMATE_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TM_API __attribute__((visibility("default")))
+#else
+#define TM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  TM_OK = 0,
+  TM_ERR_INVALID_ARGUMENT = 1, /* shape, size or count out of range */
+  TM_ERR_ALIGNMENT = 2,        /* pointer or stride misaligned for vector / TMA access */
+  TM_ERR_UNSUPPORTED = 3,      /* head dim or dtype that is not built */
+  TM_ERR_CUDA = 4,             /* CUDA runtime / driver call failed */
+  TM_ERR_DEVICE = 5            /* a kernel's bounded wait ran out (device error flag) */
+} tm_status;
+
+enum { TM_DTYPE_BF16 = 0, TM_DTYPE_F32 = 1 };
+
+/* Version of this ABI (incremented on any signature change). */
+TM_API int tm_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+TM_API const char* tm_last_error(void);
+
+/*
+ * Read and clear the device-side error flag of the current device.  Blocks
+ * until all prior work on the device has finished.  *code_out receives 0 when
+ * no kernel reported an error, 1 when a bounded wait ran out.
+ */
+TM_API int tm_device_error(int* code_out);
+
+/*
+ * A1. SPLIT-mode RoPE cos/sin tables for one batch row.
+ * Replaces causal_precompute_freqs_cis (ltx_causal/rope/causal_rope.py:139-357,
+ * called at ltx_causal/transformer/kv_cache.py:2911-3027) for rope_type=SPLIT.
+ *   grid: n_pos (1 or 3) latent extents: (F, H, W) video, (F,) audio / temporal.
+ *   theta: effective base (the caller applies NTK scaling, causal_rope.py:199-246).
+ *   max_pos: n_pos normalisers (20, 2048, 2048 for video).
+ *   repeat_per_frame: >1 expands each temporal position to that many tokens
+ *     (cross-modal PE expansion at kv_cache.py:2973-2983); 1 otherwise.
+ * Output layout: [num_heads, T, dim / 2 / num_heads], T = prod(grid) * repeat,
+ * dtype out_dtype (bf16 or fp32).  Angles are formed in fp32 in the
+ * reference's operation order; cos/sin in full-precision fp32.
+ */
+TM_API int tm_rope_tables_split(void* cos_out, void* sin_out, int out_dtype, int n_pos,
+                         const int64_t* grid, int dim, int num_heads, double theta,
+                         const double* max_pos, int64_t start_frame, int is_audio,
+                         int64_t repeat_per_frame, void* stream);
+
+/*
+ * A2+A3. Fused q/k RMSNorm (over the full H*D inner dim) + split RoPE, with
+ * the Ulysses seq->head send-buffer layout applied on the store.
+ * Replaces attn.q_norm / attn.k_norm (nn.RMSNorm, causal_attention.py:105-106,
+ * applied at kv_cache.py:1406-1407) followed by attn._apply_rope ->
+ * apply_split_rotary_emb (causal_attention.py:326, causal_rope.py:102-132),
+ * and the pack permute of _seq_to_head (taomate/runtime_support/parallel/
+ * all_to_all.py:139-140).
+ *   x:   [B, L, H*D] bf16 (token rows; row/batch strides in elements).
+ *   out: element (b, l, h, d) is stored at
+ *        out + g*out_group_stride + b*out_batch_stride + l*out_row_stride
+ *            + (h mod H/sp_size)*D + d,   g = h / (H/sp_size),
+ *        i.e. [B, L, H, D] for sp_size 1 and an all-to-all send buffer with
+ *        one head group per destination rank otherwise.
+ *   norm_weight: [H*D] bf16, or NULL for no RMSNorm.
+ *   cos/sin: [B, H, L, D/2] bf16 with the given strides, or NULL for no RoPE
+ *   (a job with neither is a pure layout copy, used for V).
+ * Up to 4 jobs (q, k, v) run in one launch.  D in {64, 128};
+ * H*D a multiple of 256 and at most 4096.  Rows must be 16-byte aligned.
+ */
+typedef struct {
+  const void* x;
+  void* out;
+  const void* norm_weight;
+  const void* cos;
+  const void* sin;
+  int64_t x_batch_stride, x_row_stride;
+  int64_t out_group_stride, out_batch_stride, out_row_stride;
+  int64_t pe_batch_stride, pe_head_stride, pe_row_stride;
+  int64_t L;
+} tm_norm_rope_job;
+
+TM_API int tm_norm_rope(const tm_norm_rope_job* jobs, int n_jobs, int B, int H, int D, float eps,
+                 int sp_size, void* stream);
+
+/*
+ * A6/A11/A12. Row-span copies for the KV slot arena: commit-time append of a
+ * chunk's K/V into a slot, compaction on eviction and materialisation of a
+ * slot list into a contiguous [B, L, H, D] tensor.
+ * Replaces the torch.cat of _cat_cache (kv_cache.py:394-398, 2642-2654) and
+ * the per-field slicing of _slice_cache / _slice_tensor
+ * (taomate/inference/cache.py:28-56).
+ * Each span copies `rows` rows of `row_bytes` bytes (strides in bytes).
+ * row_bytes, strides and pointers must be multiples of 16.  Up to 64 spans.
+ */
+typedef struct {
+  const void* src;
+  void* dst;
+  int64_t rows;
+  int64_t src_row_stride;
+  int64_t dst_row_stride;
+} tm_copy_span;
+
+TM_API int tm_copy_rows(const tm_copy_span* spans, int n_spans, int64_t row_bytes, void* stream);
+
+/*
+ * A4/A8/A13. Rank-5 strided copy with a contiguous innermost dimension: the
+ * layout permutes around the Ulysses all-to-all (_seq_to_head / _head_to_seq,
+ * all_to_all.py:125-173; cp_utils._all_to_all_swap, ltx_causal/parallel/
+ * cp_utils.py:272-345) and the SP pad/split (sp_utils.py:25-55).
+ * sizes[4] is the contiguous dimension, in elements of elem_bytes; strides in
+ * elements.  sizes[4] * elem_bytes must be a multiple of 16.
+ */
+TM_API int tm_strided_copy5(const void* src, void* dst, const int64_t* sizes,
+                     const int64_t* src_strides, const int64_t* dst_strides, int elem_bytes,
+                     void* stream);
+
+/*
+ * A7. Flash attention of a query chunk over a KV visibility list, on
+ * tcgen05 tensor cores (TMA-fed tiles, fp32 accumulators in TMEM, online
+ * softmax in registers).  Replaces the cache concat + SDPA of
+ * attention_with_cache (kv_cache.py:1486-1531) ->
+ * standard_attention_forward (ltx_causal/attention/flex_attention_utils.py:
+ * 225-276, F.scaled_dot_product_attention without mask).
+ *
+ * The visible key set is the ordered list of spans; each span names a source
+ * (TM_KV_SOURCE_CACHE: the slot arena k_cache/v_cache; TM_KV_SOURCE_NEW: the
+ * chunk's own k_new/v_new) and a row range in it.  The anchor + rolling
+ * window + current-chunk visibility is evaluated per key tile in the kernel;
+ * no mask and no concatenated K/V are materialised.
+ *   q, out: [B, Lq, H, D] bf16.  k_cache, v_cache, k_new, v_new: [B, rows, H, D] bf16.
+ *   Heads contiguous (head stride D); batch / row strides in elements,
+ *   multiples of 8 (16 bytes).  D in {64, 128}; total visible keys <= 24576.
+ */
+enum { TM_KV_SOURCE_CACHE = 0, TM_KV_SOURCE_NEW = 1 };
+
+typedef struct {
+  int32_t source;
+  int32_t row_start;
+  int32_t rows;
+} tm_kv_span;
+
+TM_API int tm_attention_fwd(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
+                     const void* k_cache, const void* v_cache, int64_t cache_batch_stride,
+                     int64_t cache_row_stride, int64_t cache_rows, const void* k_new,
+                     const void* v_new, int64_t new_batch_stride, int64_t new_row_stride,
+                     int64_t new_rows, const tm_kv_span* spans, int n_spans, void* out,
+                     int64_t out_batch_stride, int64_t out_row_stride, int B, int Lq, int H,
+                     int D, float scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TAOMATE_B200_H */

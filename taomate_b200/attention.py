@@ -1,0 +1,210 @@
+"""Streaming attention with KV cache on the sm_100a kernels.
+
+``attention_with_cache`` has the signature and return contract of
+``ltx_causal/transformer/kv_cache.py:1148-1547``; ``standard_attention_forward``
+that of ``ltx_causal/attention/flex_attention_utils.py:225-276``.
+
+Per call (video self-attention, C2 shapes):
+  1. projections ``to_q/to_k/to_v`` (cuBLAS GEMMs through torch);
+  2. ONE fused kernel: q/k RMSNorm over the inner dim + split RoPE (+ the V
+     layout copy), storing straight into the Ulysses send buffer when SP is on;
+  3. under SP, ONE NCCL all-to-all for Q, K and V together;
+  4. ONE attention kernel over [cached spans..., new chunk] read in place
+     (slot arena or plain cache tensor; no concatenation);
+  5. under SP, the head->seq all-to-all and its unpack;
+  6. optional per-head gate and ``to_out`` (torch / cuBLAS).
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Sequence, Tuple
+
+import torch
+import torch.nn.functional as F
+from torch import Tensor
+
+from . import _lib
+from . import parallel as P
+from .kv_cache import ArenaKV, cache_rows_view
+from .rope import norm_rope
+
+
+def _row_strides(t: Tensor, H: int, D: int) -> Tuple[int, int]:
+    """(batch, row) element strides of a ``[B, L, H, D]`` tensor with
+    contiguous heads."""
+    if t.dim() != 4 or t.shape[2] != H or t.shape[3] != D or t.stride(3) != 1 or t.stride(2) != D:
+        raise ValueError(f"expected [B, L, {H}, {D}] with contiguous heads, got shape "
+                         f"{tuple(t.shape)} strides {t.stride()}")
+    return (t.stride(0) if t.shape[0] > 1 else 0), t.stride(1)
+
+
+def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tensor],
+                    cache_spans: Sequence[Tuple[int, int]], new_k: Optional[Tensor],
+                    new_v: Optional[Tensor], new_rows: int, scale: Optional[float] = None,
+                    out: Optional[Tensor] = None) -> Tensor:
+    """``softmax(q K^T * scale) V`` with the keys of ``cache_spans`` (row ranges
+    of ``cache_k/v``) followed by the first ``new_rows`` rows of ``new_k/v``.
+    All tensors ``[B, L, H, D]`` bf16 with contiguous heads."""
+    dev = _lib.require_cuda(q, cache_k, new_k)
+    B, Lq, H, D = (int(v) for v in q.shape)
+    if q.dtype != torch.bfloat16:
+        raise TypeError(f"expected bfloat16, got {q.dtype}")
+    qbs, qrs = _row_strides(q, H, D)
+    if out is None:
+        out = torch.empty(B, Lq, H, D, device=dev, dtype=torch.bfloat16)
+    obs, ors = _row_strides(out, H, D)
+    spans = [(0, int(s), int(n)) for (s, n) in cache_spans if n > 0]
+    if new_k is not None and new_rows > 0:
+        spans.append((1, 0, int(new_rows)))
+    arr = (_lib.KVSpan * max(1, len(spans)))()
+    for i, (src, s, n) in enumerate(spans):
+        arr[i].source, arr[i].row_start, arr[i].rows = src, s, n
+    cbs = crs = crows = 0
+    if cache_k is not None:
+        if cache_k.dtype != torch.bfloat16 or cache_v.dtype != torch.bfloat16:
+            raise TypeError("cache must be bfloat16")
+        cbs, crs = _row_strides(cache_k, H, D)
+        if _row_strides(cache_v, H, D) != (cbs, crs):
+            raise ValueError("cached K and V must share strides")
+        crows = int(cache_k.shape[1])
+    nbs = nrs = nrows = 0
+    if new_k is not None:
+        if new_k.dtype != torch.bfloat16 or new_v.dtype != torch.bfloat16:
+            raise TypeError("new K/V must be bfloat16")
+        nbs, nrs = _row_strides(new_k, H, D)
+        if _row_strides(new_v, H, D) != (nbs, nrs):
+            raise ValueError("new K and V must share strides")
+        nrows = int(new_k.shape[1])
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(lib.tm_attention_fwd(
+            q.data_ptr(), qbs, qrs,
+            cache_k.data_ptr() if cache_k is not None else None,
+            cache_v.data_ptr() if cache_v is not None else None, cbs, crs, crows,
+            new_k.data_ptr() if new_k is not None else None,
+            new_v.data_ptr() if new_v is not None else None, nbs, nrs, nrows,
+            arr, len(spans), out.data_ptr(), obs, ors, B, Lq, H, D,
+            float(scale) if scale is not None else 0.0, _lib.stream_ptr(dev)), "attention")
+    return out
+
+
+def standard_attention_forward(q: Tensor, k: Tensor, v: Tensor, mask: Optional[Tensor] = None,
+                               scale: Optional[float] = None) -> Tensor:
+    """Unmasked SDPA on ``[B, L, H, D]`` tensors (flex_attention_utils.py:225-276)."""
+    if mask is not None:
+        raise NotImplementedError("masked attention is not on the streaming path; "
+                                  "the KV-cache path calls this with mask=None")
+    return flash_attention(q, None, None, (), k, v, int(k.shape[1]), scale)
+
+
+def _norm_eps(norm) -> float:
+    eps = getattr(norm, "eps", None)
+    return 1e-6 if eps is None else float(eps)
+
+
+def _cache_source(cached_k, cached_v):
+    """Cache tensors and row spans for the kernel (arena views read in place)."""
+    if cached_k is None:
+        return None, None, []
+    if isinstance(cached_k, ArenaKV):
+        if not isinstance(cached_v, ArenaKV) or cached_v._state is not cached_k._state:
+            raise ValueError("cached K and V arena views must belong to one pair")
+        kt, rows = cache_rows_view(cached_k)
+        return kt, cached_k.arena.v, rows
+    return cached_k, cached_v, [(0, int(cached_k.shape[1]))]
+
+
+def attention_with_cache(
+    attn,
+    x: Tensor,
+    context: Optional[Tensor],
+    pe: Optional[Tuple[Tensor, Tensor]],
+    k_pe: Optional[Tuple[Tensor, Tensor]],
+    cached_k,
+    cached_v,
+    logit_log_scale: Optional[Tensor] = None,
+    pyramid_policy=None,
+    layer_idx: Optional[int] = None,
+    modality: Optional[str] = None,
+    frame_seqlen: Optional[int] = None,
+    sp_context_sharded: bool = True,
+    new_kv_real_len: Optional[int] = None,
+    profile_name: Optional[str] = None,
+):
+    """One attention op with KV cache (kv_cache.py:1148-1547).
+
+    ``attn`` is the reference ``CausalLTXAttention`` module (or any object
+    with ``to_q/to_k/to_v/to_out[0]`` linears, ``q_norm/k_norm`` RMSNorms,
+    ``heads``, ``dim_head`` and optional ``to_gate_logits``).  ``cached_k/v``
+    are ``[B, L, H(/sp), D]`` tensors or arena views.  Returns ``(out, new_k,
+    new_v)`` with ``new_k/v`` in the cache layout (head-sharded under SP).
+    """
+    if pyramid_policy is not None:
+        raise NotImplementedError("pyramid KV selection is disabled in every shipped config")
+    B, L, _ = x.shape
+    ctx = x if context is None else context
+    H, D = int(attn.heads), int(attn.dim_head)
+    sp_size = P.get_sp_world_size() if P.is_sp_enabled() else 1
+    if sp_size > 1 and not sp_context_sharded:
+        raise NotImplementedError("text cross-attention (replicated K/V) is not on this path")
+
+    # 1. projections (library GEMMs)
+    q = F.linear(x, attn.to_q.weight, attn.to_q.bias)
+    k = F.linear(ctx, attn.to_k.weight, attn.to_k.bias)
+    v = F.linear(ctx, attn.to_v.weight, attn.to_v.bias)
+    q_pe = pe
+    kk_pe = k_pe if k_pe is not None else pe
+    eps_q, eps_k = _norm_eps(attn.q_norm), _norm_eps(attn.k_norm)
+    if abs(eps_q - eps_k) > 0:
+        raise NotImplementedError("q_norm and k_norm with different eps")
+
+    # 2-3. fused norm + RoPE (+ send layout) and the seq->head exchange
+    if sp_size == 1:
+        q, k = norm_rope([q, k], [attn.q_norm.weight, attn.k_norm.weight], [q_pe, kk_pe], H, D,
+                         eps_q)
+        v = v.view(B, -1, H, D)
+        if logit_log_scale is not None:
+            s = logit_log_scale.to(q.dtype)
+            q = q * (s.unsqueeze(-1) if s.dim() == 3 else s.view(B, -1, 1, 1))
+    else:
+        same = (q.shape == k.shape == v.shape)
+        if same:
+            send = norm_rope([q, k, v], [attn.q_norm.weight, attn.k_norm.weight, None],
+                             [q_pe, kk_pe, None], H, D, eps_q, sp_size=sp_size, packed=True)
+            q, k, v = P.seq_all_to_all_head_packed(send, P.get_sp_group(), sp_size)
+        else:
+            sq, sk, sv = norm_rope([q, k, v], [attn.q_norm.weight, attn.k_norm.weight, None],
+                                   [q_pe, kk_pe, None], H, D, eps_q, sp_size=sp_size)
+            grp = P.get_sp_group()
+            q = P._recv_to_head_layout(P._a2a(sq, grp)[0])
+            k = P._recv_to_head_layout(P._a2a(sk, grp)[0])
+            v = P._recv_to_head_layout(P._a2a(sv, grp)[0])
+        if logit_log_scale is not None:
+            s = logit_log_scale.to(q.dtype)
+            s = s.unsqueeze(-1) if s.dim() == 3 else (s if s.dim() == 4 else s.view(1, -1, 1, 1))
+            q = q * s
+
+    # real-length strip (kv_cache.py:1474-1478): the kernel reads only the real rows
+    nk_rows = int(k.shape[1])
+    if new_kv_real_len is not None and new_kv_real_len < nk_rows:
+        nk_rows = int(new_kv_real_len)
+        k = k[:, :nk_rows]
+        v = v[:, :nk_rows]
+
+    # 4. attention over [cache spans..., new chunk]
+    ck, cv, spans = _cache_source(cached_k, cached_v)
+    if q.stride(3) != 1 or q.stride(2) != D:
+        q = q.contiguous()
+    out = flash_attention(q, ck, cv, spans, k, v, nk_rows)
+
+    # 5. head -> seq
+    if sp_size > 1:
+        out = P.head_all_to_all_seq(out, P.get_sp_group(), sp_size)
+
+    # 6. gate + out projection (kv_cache.py:1680-1700)
+    out = out.reshape(B, -1, H * D)
+    if getattr(attn, "to_gate_logits", None) is not None:
+        gates = 2.0 * torch.sigmoid(attn.to_gate_logits(x))
+        out = (out.view(B, -1, H, D) * gates.unsqueeze(-1)).view(B, -1, H * D)
+    out = attn.to_out(out)
+    return out, k, v

@@ -1,0 +1,153 @@
+"""Cache segment metadata and streaming eviction (taomate/inference/cache.py).
+
+Same functions and behaviour as the reference module: a segment is a dict
+``{"block_idx", "video_tokens", "audio_tokens"}`` recorded after every clean
+commit; ``retain_streaming_context`` keeps the sink segment (``block_idx ==
+0``) and the two newest other segments, in chronological order.
+
+For arena-backed caches (:class:`taomate_b200.kv_cache.ArenaKV` fields) the
+slice is a rewrite of each view's row list: no bytes move and the evicted
+slots return to the arena once no snapshot references them.  Plain-tensor
+fields are sliced with the span-copy kernel into new tensors, as the
+reference does with ``torch.cat``.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, List, Tuple
+
+import torch
+
+from . import _lib
+from .kv_cache import ArenaKV, KVCache, LayerKVCache
+
+VIDEO_FIELDS = ("video_self_k", "video_self_v", "v2a_k", "v2a_v")
+AUDIO_FIELDS = ("audio_self_k", "audio_self_v", "a2v_k", "a2v_v")
+
+
+def cache_segments(cache: KVCache) -> List[Dict[str, int]]:
+    """Copy of the cache's segment list (cache.py:7-8)."""
+    return [dict(item) for item in getattr(cache, "segments", [])]
+
+
+def attach_segments(cache: KVCache, segments: List[Dict[str, int]]) -> KVCache:
+    """Attach a copy of ``segments`` to ``cache`` (cache.py:10-12)."""
+    cache.segments = [dict(item) for item in segments]
+    return cache
+
+
+def _segment_offsets(segments: List[Dict[str, int]]) -> List[Tuple[int, int, int, int]]:
+    """Cumulative ``(video_start, video_end, audio_start, audio_end)`` token
+    offsets per segment (cache.py:14-26)."""
+    video_offset = 0
+    audio_offset = 0
+    offsets = []
+    for segment in segments:
+        video_end = video_offset + int(segment["video_tokens"])
+        audio_end = audio_offset + int(segment["audio_tokens"])
+        offsets.append((video_offset, video_end, audio_offset, audio_end))
+        video_offset = video_end
+        audio_offset = audio_end
+    return offsets
+
+
+def retain_indices(segments: List[Dict[str, int]], recent_blocks: int = 2) -> List[int]:
+    """Segment indices kept by the streaming policy (cache.py:58-66)."""
+    if not segments:
+        raise RuntimeError("Cached inference did not attach block metadata.")
+    sink = next(index for index, item in enumerate(segments) if int(item["block_idx"]) == 0)
+    non_sink = [index for index in range(len(segments)) if index != sink]
+    recent = non_sink[-recent_blocks:] if recent_blocks > 0 else []
+    return sorted([sink, *recent])
+
+
+def _slice_tensor(tensor: torch.Tensor, spans: List[Tuple[int, int]]) -> torch.Tensor:
+    """Concatenation of ``tensor[:, s:e]`` over ``spans`` (cache.py:28-32),
+    through the span-copy kernel."""
+    pieces = [(s, e) for s, e in spans if e > s]
+    if len(pieces) == 1:
+        s, e = pieces[0]
+        return tensor[:, s:e]
+    dev = _lib.require_cuda(tensor)
+    t = tensor if tensor.stride(-1) == 1 and tensor[0, 0].is_contiguous() else tensor.contiguous()
+    B = int(t.shape[0])
+    total = sum(e - s for s, e in pieces)
+    out = torch.empty((B, total) + tuple(t.shape[2:]), dtype=t.dtype, device=dev)
+    if total == 0:
+        return out
+    row_bytes = t[0, 0].numel() * t.element_size()
+    spans_c = (_lib.CopySpan * (len(pieces) * B))()
+    i = off = 0
+    for s, e in pieces:
+        for b in range(B):
+            sp = spans_c[i]
+            sp.src = t[b, s].data_ptr()
+            sp.dst = out[b, off].data_ptr()
+            sp.rows = e - s
+            sp.src_row_stride = t.stride(1) * t.element_size()
+            sp.dst_row_stride = out.stride(1) * out.element_size()
+            i += 1
+        off += e - s
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().tm_copy_rows(spans_c, i, row_bytes, _lib.stream_ptr(dev)),
+                   "_slice_tensor")
+    return out
+
+
+def _slice_pair(k, v, spans: List[Tuple[int, int]]):
+    if k is None:
+        return None, None
+    if isinstance(k, ArenaKV):
+        if not isinstance(v, ArenaKV) or v._state is not k._state:
+            raise ValueError("K and V arena views of a pair must share their state")
+        st = k._state.sliced(spans)
+        return ArenaKV(st.arena, "k", st), ArenaKV(st.arena, "v", st)
+    return _slice_tensor(k, spans), _slice_tensor(v, spans)
+
+
+def _slice_cache(cache: KVCache, indices: List[int]) -> KVCache:
+    """Keep the segments ``indices`` of every layer field (cache.py:34-56):
+    video spans slice ``video_self_*`` and ``v2a_*``, audio spans slice
+    ``audio_self_*`` and ``a2v_*``."""
+    segments = cache_segments(cache)
+    offsets = _segment_offsets(segments)
+    video_spans = [(offsets[i][0], offsets[i][1]) for i in indices]
+    audio_spans = [(offsets[i][2], offsets[i][3]) for i in indices]
+    layers = []
+    for layer in cache.layers:
+        vk, vv = _slice_pair(layer.video_self_k, layer.video_self_v, video_spans)
+        ak, av = _slice_pair(layer.audio_self_k, layer.audio_self_v, audio_spans)
+        a2k, a2v = _slice_pair(layer.a2v_k, layer.a2v_v, audio_spans)
+        v2k, v2v = _slice_pair(layer.v2a_k, layer.v2a_v, video_spans)
+        layers.append(LayerKVCache(video_self_k=vk, video_self_v=vv, audio_self_k=ak,
+                                   audio_self_v=av, a2v_k=a2k, a2v_v=a2v, v2a_k=v2k, v2a_v=v2v))
+    return attach_segments(KVCache(layers=layers), [segments[i] for i in indices])
+
+
+def retain_streaming_context(cache: KVCache) -> KVCache:
+    """Keep the sink block and the two newest blocks (cache.py:58-67)."""
+    segments = cache_segments(cache)
+    keep = retain_indices(segments)
+    return cache if keep == list(range(len(segments))) else _slice_cache(cache, keep)
+
+
+def retain_window(cache: KVCache, anchor_tokens: int, window_tokens: int,
+                  field_names=("video_self",)) -> KVCache:
+    """Token-granular retention for arena caches: the first ``anchor_tokens``
+    rows plus the newest ``window_tokens`` rows of each listed pair (the
+    "1 anchor frame + 8 window frames" layout of the benchmark config).  No
+    data moves; segments are not tracked."""
+    layers = []
+    for layer in cache.layers:
+        kw = {f.name: getattr(layer, f.name) for f in LayerKVCache.__dataclass_fields__.values()}
+        for name in field_names:
+            k, v = kw[name + "_k"], kw[name + "_v"]
+            if k is None:
+                continue
+            L = int(k.shape[1])
+            if L <= anchor_tokens + window_tokens:
+                continue
+            spans = [(0, anchor_tokens), (L - window_tokens, L)]
+            kw[name + "_k"], kw[name + "_v"] = _slice_pair(k, v, spans)
+        layers.append(LayerKVCache(**kw))
+    return KVCache(layers=layers)

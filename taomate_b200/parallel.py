@@ -1,0 +1,377 @@
+"""Ulysses sequence parallelism for the streaming attention path.
+
+Same public API as ``taomate/runtime_support/parallel`` (mesh.py,
+all_to_all.py, sp_utils.py): a ``(dp, sp)`` device mesh, seq<->head
+all-to-all (sync, packed "many", async) and sequence split / gather.
+
+B200 design:
+* one process per GPU, NCCL ``all_to_all_single`` over NVLink / NVSwitch
+  (every peer at full bandwidth, so a flat all-to-all needs no topology
+  logic);
+* the pack permute before the seq->head exchange is done by the producing
+  kernel (the fused norm+RoPE store, see :func:`taomate_b200.rope.norm_rope`)
+  or by the strided-copy kernel; for batch 1 the receive side of seq->head
+  and the send side of head->seq are plain views (no copy);
+* Q, K and V travel in ONE collective, interleaved per token, so that after
+  the exchange Q/K/V are strided views with a uniform row stride that the
+  attention kernel's TMA maps read directly.
+
+Layout permutes run on CUDA tensors only.  A test may register a
+permute implementation for another device type (e.g. CPU ranks on gloo)
+with :func:`register_layout_copy`; the library registers none.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Callable, Dict, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+try:  # pragma: no cover - depends on the torch build
+    from torch.distributed.device_mesh import init_device_mesh, DeviceMesh
+except ImportError:  # pragma: no cover
+    init_device_mesh = None
+    DeviceMesh = None
+
+# ---------------------------------------------------------------------------
+# Mesh (mesh.py:32-160)
+# ---------------------------------------------------------------------------
+_DEVICE_MESH = None
+_SP_SIZE = 1
+_DP_SIZE = 1
+
+
+def init_sp_mesh(world_size: int, sp_size: int, device_type: str = "cuda"):
+    """Create and cache the 2-D ``(dp, sp)`` mesh; ``sp_size <= 1`` disables SP."""
+    global _DEVICE_MESH, _SP_SIZE, _DP_SIZE
+    if sp_size <= 1:
+        _DEVICE_MESH, _SP_SIZE, _DP_SIZE = None, 1, max(world_size, 1)
+        return None, _DP_SIZE, 1
+    if world_size % sp_size != 0:
+        raise ValueError(f"world_size ({world_size}) must be divisible by sp_size ({sp_size}).")
+    if init_device_mesh is None:
+        raise RuntimeError("torch.distributed.device_mesh.init_device_mesh is unavailable")
+    if not dist.is_available() or not dist.is_initialized():
+        raise RuntimeError("init_sp_mesh requires torch.distributed to be initialized first.")
+    dp_size = world_size // sp_size
+    mesh = init_device_mesh(device_type, (dp_size, sp_size), mesh_dim_names=("dp", "sp"))
+    _DEVICE_MESH, _SP_SIZE, _DP_SIZE = mesh, sp_size, dp_size
+    return mesh, dp_size, sp_size
+
+
+def get_device_mesh():
+    return _DEVICE_MESH
+
+
+def is_sp_enabled() -> bool:
+    return _DEVICE_MESH is not None and _SP_SIZE > 1
+
+
+def get_sp_group():
+    return None if _DEVICE_MESH is None else _DEVICE_MESH["sp"].get_group()
+
+
+def get_sp_world_size() -> int:
+    return _SP_SIZE
+
+
+def get_sp_rank() -> int:
+    return 0 if _DEVICE_MESH is None else int(_DEVICE_MESH["sp"].get_local_rank())
+
+
+def get_dp_group():
+    if _DEVICE_MESH is None:
+        return dist.group.WORLD if dist.is_available() and dist.is_initialized() else None
+    return _DEVICE_MESH["dp"].get_group()
+
+
+def get_dp_world_size() -> int:
+    if _DEVICE_MESH is None:
+        return dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+    return _DP_SIZE
+
+
+def get_dp_rank() -> int:
+    if _DEVICE_MESH is None:
+        return dist.get_rank() if dist.is_available() and dist.is_initialized() else 0
+    return int(_DEVICE_MESH["dp"].get_local_rank())
+
+
+# ---------------------------------------------------------------------------
+# Layout copies
+# ---------------------------------------------------------------------------
+_LAYOUT_COPY: Dict[str, Callable[[torch.Tensor, Sequence[int]], torch.Tensor]] = {}
+
+
+def register_layout_copy(device_type: str, fn: Optional[Callable]) -> None:
+    """Install (or remove with ``None``) the permute-copy used for tensors of
+    ``device_type`` other than CUDA."""
+    if fn is None:
+        _LAYOUT_COPY.pop(device_type, None)
+    else:
+        _LAYOUT_COPY[device_type] = fn
+
+
+def permute_copy(x: torch.Tensor, perm: Sequence[int]) -> torch.Tensor:
+    """Contiguous ``x.permute(perm)`` for a rank-5 tensor whose last dim stays
+    last and contiguous (one strided-copy kernel on CUDA)."""
+    if x.dim() != 5 or perm[4] != 4:
+        raise ValueError("permute_copy expects rank 5 with the innermost dim fixed")
+    if not x.is_cuda:
+        fn = _LAYOUT_COPY.get(x.device.type)
+        if fn is None:
+            raise RuntimeError(f"no layout-copy kernel for {x.device.type} tensors")
+        return fn(x, perm)
+    if x.stride(4) != 1:
+        x = x.contiguous()
+    xp = x.permute(*perm)
+    out = torch.empty(xp.shape, dtype=x.dtype, device=x.device)
+    if out.numel() == 0:
+        return out
+    sizes = (ctypes.c_int64 * 5)(*[int(v) for v in xp.shape])
+    sst = (ctypes.c_int64 * 5)(*[int(v) for v in xp.stride()])
+    dst = (ctypes.c_int64 * 5)(*[int(v) for v in out.stride()])
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().tm_strided_copy5(xp.data_ptr(), out.data_ptr(), sizes, sst, dst,
+                                                x.element_size(), _lib.stream_ptr(x.device)),
+                   "permute_copy")
+    return out
+
+
+def _a2a(send: torch.Tensor, group, async_op: bool = False):
+    recv = torch.empty_like(send)
+    work = dist.all_to_all_single(recv, send, group=group, async_op=async_op)
+    return recv, work
+
+
+def _recv_to_head_layout(recv: torch.Tensor) -> torch.Tensor:
+    """``[sp, B, S_loc, H_l, D] -> [B, sp * S_loc, H_l, D]`` (a view when B == 1)."""
+    sp, B, S_loc, Hl, D = recv.shape
+    if B == 1:
+        return recv.view(1, sp * S_loc, Hl, D)
+    return permute_copy(recv, (1, 0, 2, 3, 4)).view(B, sp * S_loc, Hl, D)
+
+
+def _seq_to_head_send(x: torch.Tensor, sp_size: int) -> torch.Tensor:
+    B, S_loc, H, D = x.shape
+    if H % sp_size != 0:
+        raise AssertionError(f"H ({H}) must be divisible by sp_size ({sp_size})")
+    return permute_copy(x.reshape(B, S_loc, sp_size, H // sp_size, D), (2, 0, 1, 3, 4))
+
+
+def _head_to_seq_send(x: torch.Tensor, sp_size: int) -> torch.Tensor:
+    B, S, Hl, D = x.shape
+    if S % sp_size != 0:
+        raise AssertionError(f"S ({S}) must be divisible by sp_size ({sp_size})")
+    if B == 1 and x.is_contiguous():
+        return x.view(sp_size, 1, S // sp_size, Hl, D)
+    return permute_copy(x.reshape(B, sp_size, S // sp_size, Hl, D), (1, 0, 2, 3, 4))
+
+
+def _recv_to_seq_layout(recv: torch.Tensor) -> torch.Tensor:
+    """``[sp, B, S_loc, H_l, D] -> [B, S_loc, sp * H_l, D]``."""
+    sp, B, S_loc, Hl, D = recv.shape
+    return permute_copy(recv, (1, 2, 0, 3, 4)).view(B, S_loc, sp * Hl, D)
+
+
+def _seq_to_head(x: torch.Tensor, sp_size: int, group) -> torch.Tensor:
+    """``[B, S/sp, H, D] -> [B, S, H/sp, D]`` (all_to_all.py:125-151)."""
+    recv, _ = _a2a(_seq_to_head_send(x, sp_size), group)
+    return _recv_to_head_layout(recv)
+
+
+def _head_to_seq(x: torch.Tensor, sp_size: int, group) -> torch.Tensor:
+    """``[B, S, H/sp, D] -> [B, S/sp, H, D]`` (all_to_all.py:154-173)."""
+    recv, _ = _a2a(_head_to_seq_send(x, sp_size), group)
+    return _recv_to_seq_layout(recv)
+
+
+# ---------------------------------------------------------------------------
+# Public all-to-all API (all_to_all.py:267-432)
+# ---------------------------------------------------------------------------
+def _resolve(group, sp_size):
+    if sp_size is None:
+        sp_size = get_sp_world_size()
+    if group is None and sp_size > 1:
+        group = get_sp_group()
+    return group, sp_size
+
+
+def seq_all_to_all_head(x: torch.Tensor, group=None, sp_size: Optional[int] = None) -> torch.Tensor:
+    """``[B, S/sp, H, D] -> [B, S, H/sp, D]``; identity when ``sp_size <= 1``."""
+    group, sp_size = _resolve(group, sp_size)
+    if sp_size <= 1:
+        return x
+    return _seq_to_head(x, sp_size, group)
+
+
+def head_all_to_all_seq(x: torch.Tensor, group=None, sp_size: Optional[int] = None) -> torch.Tensor:
+    """``[B, S, H/sp, D] -> [B, S/sp, H, D]``; identity when ``sp_size <= 1``."""
+    group, sp_size = _resolve(group, sp_size)
+    if sp_size <= 1:
+        return x
+    return _head_to_seq(x, sp_size, group)
+
+
+def seq_all_to_all_head_packed(send: torch.Tensor, group=None, sp_size: Optional[int] = None):
+    """Exchange a packed send buffer ``[sp, B, S_loc, n, H/sp, D]`` (as written
+    by ``norm_rope(..., packed=True)``) and return the ``n`` head-sharded
+    ``[B, S, H/sp, D]`` views (uniform row stride ``n * H/sp * D`` when B == 1)."""
+    group, sp_size = _resolve(group, sp_size)
+    sp, B, S_loc, n, Hl, D = send.shape
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    if B == 1:
+        flat = recv.view(sp * S_loc, n, Hl, D)
+        return tuple(flat[:, i].unsqueeze(0) for i in range(n))
+    return tuple(_recv_to_head_layout(recv[:, :, :, i]) for i in range(n))
+
+
+def seq_all_to_all_head_many(tensors, group=None, sp_size: Optional[int] = None):
+    """Packed ``seq_all_to_all_head`` for same-shaped tensors: one collective
+    (all_to_all.py:285-315)."""
+    tensors = tuple(tensors)
+    if not tensors:
+        return tuple()
+    group, sp_size = _resolve(group, sp_size)
+    if sp_size <= 1 or len(tensors) == 1:
+        return tensors if sp_size <= 1 else (seq_all_to_all_head(tensors[0], group, sp_size),)
+    base = tuple(tensors[0].shape)
+    if any(tuple(t.shape) != base for t in tensors):
+        return tuple(seq_all_to_all_head(t, group=group, sp_size=sp_size) for t in tensors)
+    B, S_loc, H, D = base
+    if H % sp_size != 0:
+        raise AssertionError(f"H ({H}) must be divisible by sp_size ({sp_size})")
+    Hl = H // sp_size
+    n = len(tensors)
+    send = torch.empty(sp_size, B, S_loc, n, Hl, D, dtype=tensors[0].dtype,
+                       device=tensors[0].device)
+    for i, t in enumerate(tensors):
+        send[:, :, :, i].copy_(_seq_to_head_send(t, sp_size))
+    return seq_all_to_all_head_packed(send, group, sp_size)
+
+
+class _AsyncAllToAll:
+    """Handle of a non-blocking exchange; ``wait()`` returns the result."""
+
+    def __init__(self, recv, work, finish):
+        self._recv, self._work, self._finish = recv, work, finish
+
+    def wait(self):
+        if self._work is not None:
+            self._work.wait()
+            self._work = None
+        return self._finish(self._recv)
+
+
+class _Immediate:
+    def __init__(self, value):
+        self.value = value
+
+    def wait(self):
+        return self.value
+
+
+def seq_all_to_all_head_async(x: torch.Tensor, group=None, sp_size: Optional[int] = None):
+    group, sp_size = _resolve(group, sp_size)
+    if sp_size <= 1:
+        return _Immediate(x)
+    recv, work = _a2a(_seq_to_head_send(x, sp_size), group, async_op=True)
+    return _AsyncAllToAll(recv, work, _recv_to_head_layout)
+
+
+def head_all_to_all_seq_async(x: torch.Tensor, group=None, sp_size: Optional[int] = None):
+    group, sp_size = _resolve(group, sp_size)
+    if sp_size <= 1:
+        return _Immediate(x)
+    recv, work = _a2a(_head_to_seq_send(x, sp_size), group, async_op=True)
+    return _AsyncAllToAll(recv, work, _recv_to_seq_layout)
+
+
+def seq_all_to_all_head_many_async(tensors, group=None, sp_size: Optional[int] = None):
+    tensors = tuple(tensors)
+    if not tensors:
+        raise ValueError("seq_all_to_all_head_many_async requires at least one tensor")
+    group, sp_size = _resolve(group, sp_size)
+    if sp_size <= 1:
+        return _Immediate(tensors)
+    if len(tensors) == 1:
+        return seq_all_to_all_head_async(tensors[0], group, sp_size)
+    if torch.is_grad_enabled():
+        raise RuntimeError("seq_all_to_all_head_many_async is inference-only")
+    base = tuple(tensors[0].shape)
+    if any(tuple(t.shape) != base for t in tensors):
+        raise ValueError("seq_all_to_all_head_many_async requires same-shaped tensors")
+    B, S_loc, H, D = base
+    Hl = H // sp_size
+    n = len(tensors)
+    send = torch.empty(sp_size, B, S_loc, n, Hl, D, dtype=tensors[0].dtype,
+                       device=tensors[0].device)
+    for i, t in enumerate(tensors):
+        send[:, :, :, i].copy_(_seq_to_head_send(t, sp_size))
+    recv = torch.empty_like(send)
+    work = dist.all_to_all_single(recv, send, group=group, async_op=True)
+
+    def finish(r):
+        if B == 1:
+            flat = r.view(sp_size * S_loc, n, Hl, D)
+            return tuple(flat[:, i].unsqueeze(0) for i in range(n))
+        return tuple(_recv_to_head_layout(r[:, :, :, i]) for i in range(n))
+
+    return _AsyncAllToAll(recv, work, finish)
+
+
+# ---------------------------------------------------------------------------
+# Sequence split / gather (sp_utils.py:25-144)
+# ---------------------------------------------------------------------------
+def pad_sequence_to_multiple(x: torch.Tensor, multiple: int, dim: int = 1,
+                             pad_value: float = 0.0) -> Tuple[torch.Tensor, int, int]:
+    S = x.shape[dim]
+    if multiple <= 1 or S % multiple == 0:
+        return x, S, S
+    pad = multiple - (S % multiple)
+    shape = list(x.shape)
+    shape[dim] = S + pad
+    out = torch.full(shape, pad_value, dtype=x.dtype, device=x.device)
+    out.narrow(dim, 0, S).copy_(x)
+    return out, S, S + pad
+
+
+def unpad_sequence(x: torch.Tensor, original_length: int, dim: int = 1) -> torch.Tensor:
+    if x.shape[dim] == original_length:
+        return x
+    return x.narrow(dim, 0, original_length).contiguous()
+
+
+def split_sequence(x: torch.Tensor, dim: int = 1, sp_rank: Optional[int] = None,
+                   sp_size: Optional[int] = None) -> torch.Tensor:
+    """Local shard along ``dim`` after right-padding with zeros to a multiple
+    of ``sp_size``."""
+    if sp_size is None:
+        sp_size = get_sp_world_size()
+    if sp_size <= 1:
+        return x
+    if sp_rank is None:
+        sp_rank = get_sp_rank()
+    x, _, S = pad_sequence_to_multiple(x, sp_size, dim)
+    chunk = S // sp_size
+    return x.narrow(dim, sp_rank * chunk, chunk).contiguous()
+
+
+def gather_sequence(x: torch.Tensor, dim: int = 1, group=None, sp_size: Optional[int] = None,
+                    sp_rank: Optional[int] = None) -> torch.Tensor:
+    """All-gather along ``dim`` over the SP group."""
+    if sp_size is None:
+        sp_size = get_sp_world_size()
+    if sp_size <= 1:
+        return x
+    if group is None:
+        group = get_sp_group()
+    x = x.contiguous()
+    parts = [torch.empty_like(x) for _ in range(sp_size)]
+    dist.all_gather(parts, x, group=group)
+    return torch.cat(parts, dim=dim)

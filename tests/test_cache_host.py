@@ -1,0 +1,104 @@
+"""Host-side cache logic without a GPU: slot reference counting, slicing of
+arena views (no data movement), the retention policy and the reference's
+error behaviour."""
+
+import pytest
+import torch
+
+from taomate_b200 import cache as C
+from taomate_b200.kv_cache import ArenaKV, KVArena, KVCache, LayerKVCache, _PairState, arena_pair
+
+
+def _arena(n_slots=6, slot_rows=8):
+    return KVArena(n_slots, slot_rows, 1, 2, 8, dtype=torch.bfloat16, device="meta")
+
+
+def _pair_with(arena, lens):
+    entries = []
+    for n in lens:
+        slot = arena._take()
+        entries.append((slot, slot * arena.slot_rows, n))
+    k, v = arena_pair(arena, entries)
+    for (slot, _, _) in entries:  # arena_pair took its own references
+        arena._ref(slot, -1)
+    return k, v
+
+
+def test_slot_refcounts_follow_views():
+    a = _arena()
+    k, v = _pair_with(a, [8, 6, 6])
+    assert a.refs[:3] == [1, 1, 1] and a.free_slots() == [3, 4, 5]
+    st = k._state.sliced([(0, 8), (14, 20)])  # keep segments 0 and 2
+    k2, v2 = ArenaKV(a, "k", st), ArenaKV(a, "v", st)
+    assert k2.shape == (1, 14, 2, 8)
+    assert [e[0] for e in k2._state.entries] == [0, 2]
+    assert a.refs[:3] == [2, 1, 2]
+    del k, v
+    assert a.refs[:3] == [1, 0, 1]
+    assert a.free_slots() == [1, 3, 4, 5]
+    del k2, v2, st
+    assert a.free_slots() == [0, 1, 2, 3, 4, 5]
+
+
+def test_slice_moves_no_rows_and_splits_entries():
+    a = _arena(slot_rows=10)
+    k, _ = _pair_with(a, [10, 9, 9])
+    st = k._state.sliced([(2, 5), (12, 25)])
+    assert st.entries == [(0, 2, 3), (1, 12, 7), (2, 20, 6)]
+    with pytest.raises(IndexError):
+        k._state.sliced([(20, 40)])
+
+
+def test_retain_streaming_context_policy_on_views():
+    a = _arena(n_slots=8, slot_rows=24)
+    vk, vv = _pair_with(a, [24, 18, 18, 18, 18])
+    layer = LayerKVCache(video_self_k=vk, video_self_v=vv)
+    segs = [{"block_idx": i, "video_tokens": n, "audio_tokens": 0}
+            for i, n in enumerate([24, 18, 18, 18, 18])]
+    cache = C.attach_segments(KVCache(layers=[layer]), segs)
+    out = C.retain_streaming_context(cache)
+    assert [s["block_idx"] for s in C.cache_segments(out)] == [0, 3, 4]
+    L = out.layers[0]
+    assert L.video_self_k.shape[1] == 24 + 18 + 18
+    assert [e[0] for e in L.video_self_k._state.entries] == [0, 3, 4]
+    assert L.video_self_k._state is L.video_self_v._state
+    # already minimal: same object back, like the reference
+    assert C.retain_streaming_context(out) is out
+
+
+def test_retain_without_segments_raises_like_reference():
+    with pytest.raises(RuntimeError, match="block metadata"):
+        C.retain_streaming_context(KVCache(layers=[]))
+
+
+def test_segment_offsets_match_oracle():
+    from oracle import ltx_oracle as O
+    segs = [{"block_idx": 0, "video_tokens": 1536, "audio_tokens": 26},
+            {"block_idx": 3, "video_tokens": 1152, "audio_tokens": 25},
+            {"block_idx": 4, "video_tokens": 1152, "audio_tokens": 25}]
+    assert C._segment_offsets(segs) == O.segment_offsets(segs)
+    for n in range(1, 8):
+        s = [{"block_idx": i, "video_tokens": 1, "audio_tokens": 1} for i in range(n)]
+        assert C.retain_indices(s) == O.retain_indices(s)
+
+
+def test_arena_full_raises():
+    a = _arena(n_slots=2)
+    _pair_with(a, [8, 8])  # views dropped immediately -> slots free again
+    k, v = _pair_with(a, [8, 8])
+    with pytest.raises(RuntimeError, match="arena full"):
+        a._take()
+    del k, v
+
+
+def test_cat_cache_requires_k_before_v():
+    from taomate_b200.kv_cache import _cat_cache
+    a = _arena()
+    k, v = _pair_with(a, [8])
+    chunk = torch.zeros(1, 4, 2, 8, dtype=torch.bfloat16, device="meta")
+    with pytest.raises(RuntimeError, match="K field"):
+        _cat_cache(v, chunk)
+    k2 = _cat_cache(k, chunk)
+    v2 = _cat_cache(v, chunk)
+    assert k2._state is v2._state and k2.shape == (1, 12, 2, 8)
+    assert k.shape == (1, 8, 2, 8)  # the old view is unchanged

@@ -1,0 +1,388 @@
+"""GPU parity tests for the sm_100a kernels (run on a B200).
+
+Tolerances:
+* RoPE tables: same fp32 angle arithmetic as the reference, so bf16 tables
+  match the reference's bf16 tables bit-for-bit except where fp32 ``pow`` of
+  two libraries differ by an ulp (< 0.5 % of entries).
+* norm + RoPE and attention kernels on identical bf16 inputs: relative L2
+  <= 2e-3 against an fp32 reference of the same op.
+* ``attention_with_cache`` end to end (bf16 projections included): no worse
+  than 1.25x the reference's own bf16 path, both measured against the
+  reference's fp32 output on the same inputs.
+* copies, slot tables and layout permutes: bit-exact.
+"""
+
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import inputs
+from oracle import ltx_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda:0") if torch.cuda.is_available() else None
+
+
+def rel_l2(a, b):
+    a = torch.as_tensor(a).double().cpu()
+    b = torch.as_tensor(b).double().cpu()
+    return float(torch.linalg.norm(a - b) / torch.linalg.norm(b))
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _device():
+    if DEV is None:
+        pytest.skip("no CUDA device")
+    torch.cuda.set_device(DEV)
+    yield
+    from taomate_b200 import _lib
+    assert _lib.device_error() == 0, "a kernel set the device error flag"
+
+
+# ---------------------------------------------------------------- A1 tables
+ROPE_CASES = ["c1_video", "c2_video", "c2_video_first", "audio", "video_cross", "c2_video_ntk"]
+
+
+@pytest.mark.parametrize("case", ROPE_CASES)
+def test_rope_tables_vs_reference(golden_dir, case):
+    import taomate_b200 as tm
+    z = np.load(os.path.join(golden_dir, "rope_tables.npz"))
+    meta = z[f"{case}__meta"]
+    n_pos = int(meta[3])
+    grid = [int(v) for v in meta[:n_pos]]
+    dim, heads, start, is_audio, ntk = (int(v) for v in meta[4:9])
+    max_pos = [float(v) for v in meta[9:9 + n_pos]]
+    rows = z[f"{case}__rows"]
+    kw = dict(theta=10000.0, max_pos=max_pos, start_frame=start, device=DEV,
+              is_audio=bool(is_audio), rope_extrapolation="ntk" if ntk else "off",
+              num_attention_heads=heads)
+    g = torch.tensor([grid])
+    c32, s32 = tm.causal_precompute_freqs_cis(g, dim, dtype=torch.float32, **kw)
+    cbf, sbf = tm.causal_precompute_freqs_cis(g, dim, dtype=torch.bfloat16, **kw)
+    c32 = c32[0].cpu().numpy()[:, rows]
+    tol = 1e-1 if ntk else 2e-3
+    np.testing.assert_allclose(c32, z[f"{case}__cos_f32"], atol=tol, rtol=0)
+    np.testing.assert_allclose(s32[0].cpu().numpy()[:, rows], z[f"{case}__sin_f32"], atol=tol,
+                               rtol=0)
+    mism = np.mean(cbf[0].float().cpu().numpy()[:, rows] != z[f"{case}__cos_bf16"])
+    assert mism < (0.08 if ntk else 0.005), mism
+    # the fp32-mirroring oracle (same angle arithmetic) agrees more tightly
+    oc, _ = O.precompute_freqs_cis_split(grid, dim, 10000.0, max_pos, start, bool(is_audio), heads,
+                                         "ntk" if ntk else "off", 8.0, precision="f32")
+    assert rel_l2(c32, oc[:, rows]) < (5e-3 if ntk else 1e-4)
+
+
+def test_rope_tables_cross_expansion():
+    import taomate_b200 as tm
+    g = torch.tensor([[3]])
+    c, s = tm.causal_precompute_freqs_cis(g, 2048, max_pos=[20], start_frame=13, device=DEV,
+                                          dtype=torch.bfloat16, num_attention_heads=32)
+    ce, se = tm.causal_precompute_freqs_cis(g, 2048, max_pos=[20], start_frame=13, device=DEV,
+                                            dtype=torch.bfloat16, num_attention_heads=32,
+                                            repeat_per_frame=384)
+    ref = c.unsqueeze(3).expand(-1, -1, -1, 384, -1).reshape(1, 32, 3 * 384, 32)
+    assert torch.equal(ce, ref)
+
+
+# ---------------------------------------------------------------- A2 + A3
+def _bf(a):
+    return torch.as_tensor(a).to(DEV, torch.bfloat16)
+
+
+@pytest.mark.parametrize("H,D,L", [(32, 128, 1152), (4, 128, 160), (32, 64, 25), (4, 64, 96)])
+def test_norm_rope_vs_oracle(H, D, L):
+    from taomate_b200.rope import norm_rope
+    import taomate_b200 as tm
+    gen = torch.Generator().manual_seed(H * 1000 + L)
+    q = torch.randn(1, L, H * D, generator=gen).to(DEV, torch.bfloat16)
+    k = (torch.randn(1, L, H * D, generator=gen) * 3.0).to(DEV, torch.bfloat16)
+    wq = torch.empty(H * D).uniform_(0.5, 1.5, generator=gen).to(DEV, torch.bfloat16)
+    wk = torch.empty(H * D).uniform_(0.5, 1.5, generator=gen).to(DEV, torch.bfloat16)
+    grid = torch.tensor([[L]]) if D == 64 else None
+    if grid is None:
+        cos, sin = torch.randn(1, H, L, D // 2, generator=gen), torch.randn(1, H, L, D // 2,
+                                                                             generator=gen)
+        nrm = torch.sqrt(cos ** 2 + sin ** 2)
+        cos, sin = (cos / nrm).to(DEV, torch.bfloat16), (sin / nrm).to(DEV, torch.bfloat16)
+    else:
+        cos, sin = tm.causal_precompute_freqs_cis(grid, H * D, max_pos=[20], device=DEV,
+                                                  dtype=torch.bfloat16, is_audio=True,
+                                                  num_attention_heads=H)
+    oq, ok = norm_rope([q, k], [wq, wk], [(cos, sin), (cos, sin)], H, D, 1e-6)
+    f = lambda t: t.float().cpu().numpy()
+    for x, w, o in ((q, wq, oq), (k, wk, ok)):
+        ref = O.apply_split_rotary_emb(O.rms_norm(f(x[0]), f(w), 1e-6), f(cos[0]), f(sin[0]))
+        assert o.shape == (1, L, H, D)
+        assert rel_l2(o[0].reshape(L, H * D), ref) < 2e-3
+
+
+def test_apply_split_rotary_vs_reference(golden_dir):
+    import taomate_b200 as tm
+    z = np.load(os.path.join(golden_dir, "split_rope.npz"))
+    x = _bf(inputs.split_rope_inputs())[None]
+    cos, sin = tm.causal_precompute_freqs_cis(torch.tensor([[1, 8, 12]]), 256, start_frame=6,
+                                              device=DEV, dtype=torch.bfloat16,
+                                              num_attention_heads=4)
+    y = tm.apply_split_rotary_emb(x, cos, sin)
+    assert y.shape == (1, 96, 256)
+    # vs the reference's fp32 run and its own bf16 run
+    assert rel_l2(y[0], z["y_f32"]) < 4e-3
+    assert rel_l2(y[0], z["y_bf16"]) < 8e-3
+
+
+@pytest.mark.parametrize("sp", [2, 4, 8])
+def test_norm_rope_packed_send_layout(sp):
+    """The store into the Ulysses send buffer is the permutation of
+    _seq_to_head's pack (all_to_all.py:139-140), bit-exact."""
+    from taomate_b200.rope import norm_rope
+    H, D, L = 32, 128, 144
+    gen = torch.Generator().manual_seed(sp)
+    xs = [torch.randn(1, L, H * D, generator=gen).to(DEV, torch.bfloat16) for _ in range(3)]
+    plain = norm_rope(xs, [None] * 3, [None] * 3, H, D, 1e-6)
+    buf = norm_rope(xs, [None] * 3, [None] * 3, H, D, 1e-6, sp_size=sp, packed=True)
+    assert buf.shape == (sp, 1, L, 3, H // sp, D)
+    for i in range(3):
+        ref = plain[i].reshape(1, L, sp, H // sp, D).permute(2, 0, 1, 3, 4)
+        assert torch.equal(buf[:, :, :, i], ref)
+
+
+# ---------------------------------------------------------------- A7 attention
+def _sdpa_ref(q, ks, vs, scale=None):
+    """fp32 SDPA on the GPU over the concatenated keys (same bf16 inputs)."""
+    k = torch.cat(ks, dim=1).float()
+    v = torch.cat(vs, dim=1).float()
+    o = torch.nn.functional.scaled_dot_product_attention(
+        q.float().transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), scale=scale)
+    return o.transpose(1, 2)
+
+
+ATTN_SHAPES = [
+    # (H, D, Lq, cache_spans (start, rows) in a cache of cache_rows, new_rows)
+    (32, 128, 1152, 3456, [(0, 3456)], 1152),            # C2: 1 anchor + 8 window frames
+    (32, 128, 1152, 6144, [(0, 384), (1536, 3072)], 1152),  # anchor + window from a slot arena
+    (4, 128, 160, 300, [(0, 300)], 160),                 # ragged lengths
+    (32, 64, 25, 101, [(0, 101)], 25),                   # audio self-attention
+    (32, 64, 1152, 101, [(0, 101)], 25),                 # A2V: video queries, audio keys
+    (32, 64, 25, 0, [], 4608),                           # V2A: audio queries, video keys
+    (4, 64, 96, 576, [(0, 576)], 96),                    # C1 shapes
+    (2, 128, 1, 7, [(0, 7)], 1),                         # single query, 8 keys
+    (8, 128, 300, 1000, [(5, 3), (100, 129), (400, 255)], 17),  # odd spans
+]
+
+
+@pytest.mark.parametrize("H,D,Lq,crows,spans,nrows", ATTN_SHAPES)
+def test_flash_attention_vs_fp32(H, D, Lq, crows, spans, nrows):
+    from taomate_b200 import flash_attention
+    gen = torch.Generator().manual_seed(H + D + Lq + crows)
+    q = torch.randn(1, Lq, H, D, generator=gen).to(DEV, torch.bfloat16)
+    ck = torch.randn(1, max(crows, 1), H, D, generator=gen).to(DEV, torch.bfloat16)
+    cv = torch.randn(1, max(crows, 1), H, D, generator=gen).to(DEV, torch.bfloat16)
+    nk = torch.randn(1, nrows, H, D, generator=gen).to(DEV, torch.bfloat16)
+    nv = torch.randn(1, nrows, H, D, generator=gen).to(DEV, torch.bfloat16)
+    out = flash_attention(q, ck if crows else None, cv if crows else None, spans, nk, nv, nrows)
+    ks = [ck[:, s:s + n] for s, n in spans] + [nk]
+    vs = [cv[:, s:s + n] for s, n in spans] + [nv]
+    ref = _sdpa_ref(q, ks, vs)
+    assert torch.isfinite(out).all()
+    assert rel_l2(out, ref) < 2e-3
+    # and against the reference's own GPU path: torch SDPA in bf16 on the concatenation
+    refb = torch.nn.functional.scaled_dot_product_attention(
+        q.transpose(1, 2), torch.cat(ks, 1).transpose(1, 2), torch.cat(vs, 1).transpose(1, 2))
+    assert rel_l2(out, refb.transpose(1, 2)) < 4e-3
+
+
+def test_flash_attention_large_logits():
+    """Scores far apart exercise the lazy rescale (max grows by > 2^8)."""
+    from taomate_b200 import flash_attention
+    gen = torch.Generator().manual_seed(7)
+    H, D, Lq, Lk = 4, 128, 256, 1024
+    q = (torch.randn(1, Lq, H, D, generator=gen) * 4).to(DEV, torch.bfloat16)
+    k = torch.randn(1, Lk, H, D, generator=gen)
+    k[:, 700:] *= 6.0  # later tiles carry much larger scores
+    k = k.to(DEV, torch.bfloat16)
+    v = torch.randn(1, Lk, H, D, generator=gen).to(DEV, torch.bfloat16)
+    out = flash_attention(q, None, None, [], k, v, Lk)
+    ref = _sdpa_ref(q, [k], [v])
+    assert rel_l2(out, ref) < 2e-3
+
+
+def test_standard_attention_forward_matches_sdpa():
+    import taomate_b200 as tm
+    gen = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(2, n, 8, 64, generator=gen).to(DEV, torch.bfloat16)
+               for n in (200, 333, 333))
+    out = tm.standard_attention_forward(q, k, v)
+    ref = torch.stack([_sdpa_ref(q[b:b + 1], [k[b:b + 1]], [v[b:b + 1]])[0] for b in range(2)])
+    assert rel_l2(out, ref) < 2e-3
+    with pytest.raises(NotImplementedError):
+        tm.standard_attention_forward(q, k, v, mask=torch.ones(200, 333, dtype=torch.bool))
+
+
+def test_attention_rejects_bad_arguments():
+    from taomate_b200 import flash_attention
+    q = torch.zeros(1, 8, 2, 96, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(NotImplementedError):
+        flash_attention(q, None, None, [], q, q, 8)
+    q = torch.zeros(1, 8, 2, 64, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        flash_attention(q, q, q, [(4, 8)], q, q, 8)  # span past the cache end
+
+
+# ---------------------------------------------------------------- end to end
+class _Lin(torch.nn.Module):
+    def __init__(self, w, b):
+        super().__init__()
+        self.weight = torch.nn.Parameter(torch.from_numpy(w).to(DEV, torch.bfloat16))
+        self.bias = torch.nn.Parameter(torch.from_numpy(b).to(DEV, torch.bfloat16))
+
+    def forward(self, x):
+        return torch.nn.functional.linear(x, self.weight, self.bias)
+
+
+def make_attn(d):
+    c, p = d["cfg"], d["params"]
+    H, D = c["heads"], c["dim_head"]
+    attn = torch.nn.Module()
+    attn.heads, attn.dim_head = H, D
+    attn.to_q = _Lin(p["to_q_w"], p["to_q_b"])
+    attn.to_k = _Lin(p["to_k_w"], p["to_k_b"])
+    attn.to_v = _Lin(p["to_v_w"], p["to_v_b"])
+    attn.to_out = torch.nn.Sequential(_Lin(p["to_out_w"], p["to_out_b"]))
+    attn.q_norm = torch.nn.RMSNorm(H * D, eps=1e-6).to(DEV, torch.bfloat16)
+    attn.k_norm = torch.nn.RMSNorm(H * D, eps=1e-6).to(DEV, torch.bfloat16)
+    with torch.no_grad():
+        attn.q_norm.weight.copy_(torch.from_numpy(p["q_norm_w"]))
+        attn.k_norm.weight.copy_(torch.from_numpy(p["k_norm_w"]))
+    attn.to_gate_logits = (_Lin(p["to_gate_logits_w"], p["to_gate_logits_b"])
+                           if c["gated"] else None)
+    return attn
+
+
+@pytest.mark.parametrize("case", list(inputs.ATTN_CASES))
+def test_attention_with_cache_vs_reference(golden_dir, case):
+    import taomate_b200 as tm
+    z = np.load(os.path.join(golden_dir, f"attn_{case}.npz"))
+    d = inputs.attn_case_inputs(case)
+    c = d["cfg"]
+    attn = make_attn(d)
+    x = _bf(d["x"])[None]
+    pe = (_bf(z["cos_f32"])[None], _bf(z["sin_f32"])[None])
+    ck = _bf(d["cached_k"])[None] if d["cached_k"] is not None else None
+    cv = _bf(d["cached_v"])[None] if d["cached_v"] is not None else None
+    with torch.no_grad():
+        out, nk, nv = tm.attention_with_cache(attn, x, None, pe, None, ck, cv,
+                                              new_kv_real_len=c["real_len"])
+    assert out.shape == (1, c["lq"], c["hidden"])
+    real = c["real_len"] or c["lq"]
+    assert nk.shape == (1, real, c["heads"], c["dim_head"])
+    ref_err_out = rel_l2(z["out_bf16"], z["out_f32"])
+    ref_err_k = rel_l2(z["new_k_bf16"], z["new_k_f32"])
+    assert rel_l2(out[0], z["out_f32"]) < 1.25 * ref_err_out
+    assert rel_l2(nk[0], z["new_k_f32"]) < 1.25 * ref_err_k
+    assert rel_l2(nv[0], z["new_v_f32"]) < 1.25 * rel_l2(z["new_v_bf16"], z["new_v_f32"])
+
+
+# ---------------------------------------------------------------- copies and arena
+def test_cat_tensors_bit_exact():
+    from taomate_b200.kv_cache import cat_tensors
+    a = torch.randn(1, 333, 32, 128, device=DEV).bfloat16()
+    b = torch.randn(1, 77, 32, 128, device=DEV).bfloat16()
+    assert torch.equal(cat_tensors(a, b), torch.cat([a, b], 1))
+
+
+@pytest.mark.parametrize("perm", [(2, 0, 1, 3, 4), (1, 0, 2, 3, 4), (1, 2, 0, 3, 4)])
+def test_permute_copy_bit_exact(perm):
+    from taomate_b200.parallel import permute_copy
+    x = torch.randn(2, 3, 5, 4, 64, device=DEV).bfloat16()
+    assert torch.equal(permute_copy(x, perm), x.permute(*perm).contiguous())
+
+
+def test_arena_streaming_schedule_bit_exact(golden_dir):
+    """Replay 60 committed blocks through arena views: after every commit and
+    eviction the retained tokens equal the reference's, bit-exact, and the
+    evicted slots are reused (no growth)."""
+    import json
+    import taomate_b200 as tm
+    from taomate_b200.kv_cache import ArenaSpec, init_arena_cache
+    with open(os.path.join(golden_dir, "cache_schedule.json")) as fh:
+        g = json.load(fh)
+    ft = g["frame_tokens"]
+    cache = init_arena_cache(1, {"video_self": ArenaSpec(6, 4 * ft, 1, 8),
+                                 "audio_self": ArenaSpec(6, 32, 1, 8),
+                                 "a2v": ArenaSpec(6, 32, 1, 8), "v2a": ArenaSpec(6, 4 * ft, 1, 8)},
+                             device=DEV)
+    segs = []
+    hist = []
+    v_next = a_next = 0
+    for bi, (idx, vs, ve, as_, ae) in enumerate(g["blocks"]):
+        nv, na = (ve - vs) * ft, ae - as_
+        vid = torch.arange(v_next, v_next + nv, device=DEV).float().view(1, nv, 1, 1)
+        aud = torch.arange(a_next, a_next + na, device=DEV).float().view(1, na, 1, 1)
+        v_next += nv
+        a_next += na
+        vid8, aud8 = vid.expand(1, nv, 1, 8).bfloat16(), aud.expand(1, na, 1, 8).bfloat16()
+        L = cache.layers[0]
+        vk, vvv = tm._cat_cache(L.video_self_k, vid8), None
+        vvv = tm._cat_cache(L.video_self_v, -vid8)
+        ak = tm._cat_cache(L.audio_self_k, aud8)
+        av = tm._cat_cache(L.audio_self_v, -aud8)
+        a2k = tm._cat_cache(L.a2v_k, aud8)
+        a2v = tm._cat_cache(L.a2v_v, -aud8)
+        v2k = tm._cat_cache(L.v2a_k, vid8)
+        v2v = tm._cat_cache(L.v2a_v, -vid8)
+        layer = tm.LayerKVCache(vk, vvv, ak, av, a2k, a2v, v2k, v2v)
+        segs.append({"block_idx": idx, "video_tokens": nv, "audio_tokens": na})
+        cache = tm.attach_segments(tm.KVCache(layers=[layer]), segs)
+        if bi // 5 > 0 or bi == 4:
+            if bi == 4:
+                hist.append((layer.video_self_k.materialize(), layer.audio_self_k.materialize()))
+            cache = tm.retain_streaming_context(cache)
+        segs = tm.cache_segments(cache)
+        L = cache.layers[0]
+        hist.append((L.video_self_k.materialize(), L.audio_self_k.materialize()))
+        assert torch.equal(L.video_self_v.materialize(), -hist[-1][0])
+        assert torch.equal(L.v2a_v.materialize(), -hist[-1][0])
+        assert torch.equal(L.a2v_k.materialize(), hist[-1][1])
+        del layer, vk, vvv, ak, av, a2k, a2v, v2k, v2v
+    assert len(hist) == len(g["video_token_ids"])
+    for (vt, at), gv, ga in zip(hist, g["video_token_ids"], g["audio_token_ids"]):
+        assert vt[0, :, 0, 0].float().cpu().tolist() == [float(t) for t in gv]
+        assert at[0, :, 0, 0].float().cpu().tolist() == [float(t) for t in ga]
+    arena = cache.layers[0].video_self_k.arena
+    assert arena.n_slots == 6 and len(arena.free_slots()) >= 3
+
+
+def test_arena_attention_matches_tensor_cache():
+    """Attention over an arena view (anchor + window spans read in place)
+    equals attention over the same keys as one contiguous tensor."""
+    import taomate_b200 as tm
+    from taomate_b200.kv_cache import ArenaSpec, init_arena_cache
+    H, D = 32, 128
+    cache = init_arena_cache(1, {"video_self": ArenaSpec(6, 1536, H, D)}, device=DEV)
+    gen = torch.Generator().manual_seed(11)
+    L = cache.layers[0]
+    k, v = L.video_self_k, L.video_self_v
+    for n in (1536, 1152, 1152, 1152):
+        ck = torch.randn(1, n, H, D, generator=gen).to(DEV, torch.bfloat16)
+        cv = torch.randn(1, n, H, D, generator=gen).to(DEV, torch.bfloat16)
+        k, v = tm.cat_cache_pair(k, v, ck, cv)
+    segs = [{"block_idx": i, "video_tokens": n, "audio_tokens": 0}
+            for i, n in enumerate((1536, 1152, 1152, 1152))]
+    kc = tm.attach_segments(tm.KVCache(layers=[tm.LayerKVCache(video_self_k=k, video_self_v=v)]),
+                            segs)
+    kc = tm.retain_streaming_context(kc)
+    k, v = kc.layers[0].video_self_k, kc.layers[0].video_self_v
+    assert k.shape == (1, 1536 + 2304, H, D)
+    q = torch.randn(1, 1152, H, D, generator=gen).to(DEV, torch.bfloat16)
+    nk = torch.randn(1, 1152, H, D, generator=gen).to(DEV, torch.bfloat16)
+    nv = torch.randn(1, 1152, H, D, generator=gen).to(DEV, torch.bfloat16)
+    from taomate_b200.attention import _cache_source
+    ck, cv, spans = _cache_source(k, v)
+    out = tm.flash_attention(q, ck, cv, spans, nk, nv, 1152)
+    km, vm = k.materialize(), v.materialize()
+    ref = _sdpa_ref(q, [km, nk], [vm, nv])
+    assert rel_l2(out, ref) < 2e-3
