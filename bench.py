@@ -1,0 +1,392 @@
+#!/usr/bin/env python
+"""Benchmark of the causal-LTX streaming attention step on B200.
+
+One step = one streaming block (3 latent frames, 512x768 -> 16x24 = 384
+tokens per frame): for each of 48 layers, the video self-attention of the 3
+denoising forwards and the sigma=0 commit forward (taomate/inference/
+model.py:166-248), i.e. 192 ``attention_with_cache`` calls, followed by the
+commit append and the anchor + rolling-window eviction.  Shapes follow
+hidden 4096 = 32 heads x 128, query chunk 1152 tokens,
+cache = 1 anchor frame + 8 window frames = 3456 tokens, so every attention
+sees 4608 keys.  Weights are random N(0, 0.02), activations N(0, 1).
+
+  value  latent frames/s with all inputs resident in HBM (device time,
+         CUDA events, max over ranks);
+  e2e    the same through the public API with the step's inputs copied from
+         pinned host memory and the outputs read back, inside the timed region.
+
+With --gpus N the step runs with Ulysses sequence parallelism over N ranks
+(each rank holds 1152/N query tokens and 32/N heads of the cache): total work
+per step is fixed, so scaling is "strong".
+
+``--impl reference`` times the reference algorithm's CPU restatement
+(oracle/ltx_oracle.py, numpy fp32, all host threads) on a bounded sample of
+the same workload and reports the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FRAME_TOKENS = 16 * 24
+Q_FRAMES = 3
+ANCHOR_FRAMES = 1
+WINDOW_FRAMES = 8
+HIDDEN, HEADS, DIM_HEAD = 4096, 32, 128
+FORWARDS_PER_STEP = 4  # 3 denoising + 1 commit
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.path = tempfile.mktemp(suffix=".csv")
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, smax, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as fh:
+            for line in fh:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax = float(parts[2])
+                    power.append(float(parts[3]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "power_w_max": max(power) if power else None, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            d = json.load(fh)
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def profiled_traffic():
+    """Per-launch DRAM bytes of the attention kernel from the committed ncu
+    summary (profiles/attention_c2.md), or None."""
+    p = os.path.join(ROOT, "profiles", "attention_c2.md")
+    if not os.path.exists(p):
+        return None
+    with open(p) as fh:
+        m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", fh.read())
+    return float(m.group(1)) if m else None
+
+
+# --------------------------------------------------------------------------- CPU
+def cpu_sample_time(reps: int, warm: int):
+    """Seconds per video self-attention layer-forward (C2 shapes) of the numpy
+    fp32 restatement, min over ``reps`` after ``warm`` untimed runs."""
+    import numpy as np
+    from oracle import ltx_oracle as O
+    rng = np.random.default_rng(0)
+    f32 = np.float32
+    prm = {n: (rng.standard_normal((HIDDEN, HIDDEN)) * 0.02).astype(f32)
+           for n in ("to_q_w", "to_k_w", "to_v_w", "to_out_w")}
+    for n in ("to_q_b", "to_k_b", "to_v_b", "to_out_b"):
+        prm[n] = (rng.standard_normal(HIDDEN) * 0.02).astype(f32)
+    prm["q_norm_w"] = np.ones(HIDDEN, f32)
+    prm["k_norm_w"] = np.ones(HIDDEN, f32)
+    Lq = Q_FRAMES * FRAME_TOKENS
+    Lc = (ANCHOR_FRAMES + WINDOW_FRAMES) * FRAME_TOKENS
+    x = rng.standard_normal((Lq, HIDDEN)).astype(f32)
+    ck = rng.standard_normal((Lc, HEADS, DIM_HEAD)).astype(f32)
+    cv = rng.standard_normal((Lc, HEADS, DIM_HEAD)).astype(f32)
+    cos, sin = O.precompute_freqs_cis_split((Q_FRAMES, 16, 24), HIDDEN, start_frame=9,
+                                            num_heads=HEADS, precision="f32")
+    cos, sin = cos.astype(f32), sin.astype(f32)
+    times = []
+    for i in range(warm + reps):
+        t0 = time.perf_counter()
+        O.attention_with_cache(x, prm, HEADS, DIM_HEAD, (cos, sin), ck, cv, dtype=f32)
+        dt = time.perf_counter() - t0
+        if i >= warm:
+            times.append(dt)
+    return times
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = max((int(i.get("num_threads", 1)) for i in threadpool_info()), default=1)
+        return n
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return
+    times = cpu_sample_time(max(1, args.steps), max(0, args.warmup))
+    t = statistics.mean(times)
+    per_step = t * args.layers * FORWARDS_PER_STEP
+    value = Q_FRAMES / per_step
+    line = {
+        "metric": "latent frames/s at 512x768 (48-layer video self-attention step)",
+        "value": value, "unit": "latent frames/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "C2 video self-attention (1152 q tokens, 3456 cached, 4608 keys), "
+                               "48 layers x 4 forwards per 3-frame block",
+                   "sample": "one layer-forward per timed step, extrapolated x192"},
+        "cpu_baseline": {"value": value, "unit": "latent frames/s", "cores": cpu_threads(),
+                         "kind": "port",
+                         "sample": f"{len(times)} C2 layer-forwards (attention_with_cache incl. "
+                                   f"projections), numpy fp32, mean {t:.3f} s each"},
+        "e2e": {"value": value, "unit": "latent frames/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import taomate_b200 as tm
+    from taomate_b200 import _lib, parallel as P
+    from taomate_b200.attention import AttentionWeights
+    from taomate_b200.cache import retain_window
+    from taomate_b200.kv_cache import ArenaSpec, KVCache, LayerKVCache, init_arena_cache
+    from taomate_b200.profiler import TIMER
+
+    rank, world, local = env_rank()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        P.init_sp_mesh(world, world)
+    sp = world
+    L = args.layers
+    Lq = Q_FRAMES * FRAME_TOKENS
+    if Lq % sp or HEADS % sp:
+        raise SystemExit(f"{sp} ranks do not divide {Lq} tokens / {HEADS} heads")
+    S_loc, H_loc = Lq // sp, HEADS // sp
+    anchor, window = ANCHOR_FRAMES * FRAME_TOKENS, WINDOW_FRAMES * FRAME_TOKENS
+
+    torch.manual_seed(0)  # identical weights on every rank
+    attn = [AttentionWeights(HIDDEN, HEADS, DIM_HEAD, device=dev) for _ in range(L)]
+    gen = torch.Generator(device=dev).manual_seed(1)
+    xs = [torch.randn(1, Lq, HIDDEN, device=dev, generator=gen).to(torch.bfloat16)
+          [:, rank * S_loc:(rank + 1) * S_loc].contiguous() for _ in range(L)]
+
+    def fresh_cache():
+        return init_arena_cache(L, {"video_self": ArenaSpec(6, Lq, H_loc, DIM_HEAD)}, device=dev)
+
+    grid = torch.tensor([[Q_FRAMES, 16, 24]])
+
+    def step(cache, block, x_in=None, outs=None):
+        start = block * Q_FRAMES
+        for fwd in range(FORWARDS_PER_STEP):
+            cos, sin = tm.causal_precompute_freqs_cis(grid, HIDDEN, start_frame=start, device=dev,
+                                                      dtype=torch.bfloat16,
+                                                      num_attention_heads=HEADS)
+            pe = (cos[:, :, rank * S_loc:(rank + 1) * S_loc],
+                  sin[:, :, rank * S_loc:(rank + 1) * S_loc])
+            commit = fwd == FORWARDS_PER_STEP - 1
+            new_layers = []
+            out = None
+            for li in range(L):
+                lay = cache.layers[li]
+                x = xs[li] if x_in is None else x_in[li]
+                out, nk, nv = tm.attention_with_cache(attn[li], x, None, pe, None,
+                                                      lay.video_self_k, lay.video_self_v,
+                                                      profile_name="video_self")
+                if commit:
+                    k2, v2 = tm.cat_cache_pair(lay.video_self_k, lay.video_self_v, nk, nv)
+                    new_layers.append(LayerKVCache(video_self_k=k2, video_self_v=v2))
+            if outs is not None:
+                outs[fwd].copy_(out, non_blocking=True)
+            if commit:
+                cache = retain_window(KVCache(layers=new_layers), anchor, window)
+        return cache
+
+    def timed(n_steps, n_warm, host_io):
+        cache = fresh_cache()
+        x_host = outs = None
+        if host_io:
+            x_host = [x.cpu().pin_memory() for x in xs]
+            x_dev = [torch.empty_like(x) for x in xs]
+            outs = [torch.empty(1, S_loc, HIDDEN, dtype=torch.bfloat16).pin_memory()
+                    for _ in range(FORWARDS_PER_STEP)]
+        block = 0
+        with torch.no_grad():
+            for _ in range(n_warm):
+                cache = step(cache, block)
+                block += 1
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        l0 = _lib.LAUNCHES
+        if not host_io:
+            TIMER.start()
+        sampler = ClockSampler(local)
+        sampler.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        with torch.no_grad():
+            for _ in range(n_steps):
+                if host_io:
+                    for li in range(L):
+                        x_dev[li].copy_(x_host[li], non_blocking=True)
+                    cache = step(cache, block, x_dev, outs)
+                else:
+                    cache = step(cache, block)
+                block += 1
+        e1.record()
+        torch.cuda.synchronize()
+        clocks = sampler.stop()
+        TIMER.stop()
+        launches = _lib.LAUNCHES - l0
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            dist.barrier()
+        h2d = sum(x.numel() * x.element_size() for x in xs) if host_io else 0
+        d2h = FORWARDS_PER_STEP * S_loc * HIDDEN * 2 if host_io else 0
+        return ms, launches, clocks, h2d, d2h
+
+    ms, launches, clocks, _, _ = timed(args.steps, args.warmup, host_io=False)
+    sections = TIMER.summary()
+    value = Q_FRAMES * args.steps / (ms / 1e3)
+
+    e2e = None
+    if not args.no_e2e:
+        ems, _, _, h2d, d2h = timed(args.steps, args.warmup, host_io=True)
+        e2e = {"value": Q_FRAMES * args.steps / (ems / 1e3), "unit": "latent frames/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": ems / args.steps}
+
+    peaks, peak_kind = measured_peaks()
+    sd = sections.get("video_self.sdpa")
+    Lkv = anchor + window + Lq
+    flops = 4.0 * Lq * Lkv * H_loc * DIM_HEAD
+    roof = None
+    if sd:
+        achieved = flops / (sd["mean_ms"] * 1e-3) / 1e12
+        peak = float(peaks["bf16_tflops_sustained"])
+        traffic = profiled_traffic()
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": traffic,
+                "kernel": "tm attention (tcgen05)", "launch_ms": sd["mean_ms"],
+                "flops_per_launch": flops,
+                "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        times = cpu_sample_time(2, 1)
+        t = min(times)
+        cpu = {"value": Q_FRAMES / (t * L * FORWARDS_PER_STEP), "unit": "latent frames/s",
+               "cores": cpu_threads(), "kind": "port",
+               "sample": f"2 C2 layer-forwards of the numpy fp32 restatement "
+                         f"(attention_with_cache incl. projections), min {t:.3f} s, x{L * 4}"}
+
+    if rank == 0:
+        line = {
+            "metric": "latent frames/s at 512x768 (48-layer video self-attention step)",
+            "value": value, "unit": "latent frames/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "C2 video self-attention, 48 layers x (3 denoise + 1 commit) "
+                                   "forwards per 3-frame block",
+                       "layers": L, "q_tokens": Lq, "cached_tokens": anchor + window,
+                       "keys_per_query": Lkv, "heads": HEADS, "dim_head": DIM_HEAD,
+                       "parallelism": f"ulysses sp{sp}" if sp > 1 else "single gpu",
+                       "l2": "inputs larger than L2 (48 layers of weights, caches and "
+                             "activations, ~14 GB), no flush"},
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+            "clocks": clocks,
+            "sections_ms_per_call": {k: v["mean_ms"] for k, v in sections.items()},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -182,11 +182,12 @@ def expand_per_frame(table: np.ndarray, frame_seqlen: int) -> np.ndarray:
 def rms_norm(x: np.ndarray, weight: Optional[np.ndarray], eps: float = 1e-6) -> np.ndarray:
     """``x / sqrt(mean(x^2) + eps) * w`` over the last dim (torch.nn.RMSNorm,
     used as q_norm/k_norm at ltx_causal/attention/causal_attention.py:105-106)."""
-    x = np.asarray(x, dtype=np.float64)
-    r = 1.0 / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps)
+    dt = np.float32 if isinstance(x, np.ndarray) and x.dtype == np.float32 else np.float64
+    x = np.asarray(x, dtype=dt)
+    r = 1.0 / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + dt(eps))
     y = x * r
     if weight is not None:
-        y = y * np.asarray(weight, dtype=np.float64)
+        y = y * np.asarray(weight, dtype=dt)
     return y
 
 
@@ -197,7 +198,8 @@ def apply_split_rotary_emb(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> n
     first/second half of each head: ``out1 = x1 cos - x2 sin``,
     ``out2 = x2 cos + x1 sin``.
     """
-    x = np.asarray(x, dtype=np.float64)
+    x = np.asarray(x, dtype=x.dtype if isinstance(x, np.ndarray) and x.dtype == np.float32
+                   else np.float64)
     H, T, half = cos.shape
     xh = x.reshape(T, H, 2, half).transpose(1, 0, 2, 3)  # [H, T, 2, half]
     x1, x2 = xh[:, :, 0], xh[:, :, 1]
@@ -211,7 +213,7 @@ def apply_split_rotary_emb(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> n
 # A7: attention core
 # ----------------------------------------------------------------------------
 def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: Optional[float] = None,
-              mask: Optional[np.ndarray] = None) -> np.ndarray:
+              mask: Optional[np.ndarray] = None, dtype=np.float64) -> np.ndarray:
     """``softmax(q k^T * scale [+ mask]) v`` per head, layout ``[L, H, D]``.
 
     Restates ``standard_attention_forward`` (ltx_causal/attention/
@@ -219,12 +221,22 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: Optional[float
     with ``is_causal=False`` and default scale ``D ** -0.5``.  ``mask`` is a
     boolean ``[Lq, Lk]`` (True = visible) or additive float mask.
     """
-    q = np.asarray(q, dtype=np.float64)
-    k = np.asarray(k, dtype=np.float64)
-    v = np.asarray(v, dtype=np.float64)
+    q = np.asarray(q, dtype=dtype)
+    k = np.asarray(k, dtype=dtype)
+    v = np.asarray(v, dtype=dtype)
     D = q.shape[-1]
     if scale is None:
         scale = 1.0 / math.sqrt(D)
+    if mask is None and dtype != np.float64:
+        # head-by-head BLAS products (the fp32 path times the CPU baseline)
+        out = np.empty_like(q)
+        for h in range(q.shape[1]):
+            s = (q[:, h] @ k[:, h].T) * dtype(scale)
+            s -= s.max(axis=-1, keepdims=True)
+            np.exp(s, out=s)
+            s /= s.sum(axis=-1, keepdims=True)
+            out[:, h] = s @ v[:, h]
+        return out
     s = np.einsum("qhd,khd->hqk", q, k) * scale
     if mask is not None:
         if mask.dtype == bool:
@@ -243,7 +255,7 @@ def attention_with_cache(x: np.ndarray, params: Dict[str, np.ndarray], heads: in
                          context: Optional[np.ndarray] = None,
                          k_pe: Optional[Tuple[np.ndarray, np.ndarray]] = None,
                          new_kv_real_len: Optional[int] = None,
-                         eps: float = 1e-6):
+                         eps: float = 1e-6, dtype=np.float64):
     """Single-rank ``attention_with_cache`` (ltx_causal/transformer/kv_cache.py:1148-1547).
 
     ``x``: ``[L, Dq]`` (batch 1); ``params``: ``to_q/to_k/to_v/to_out`` weight
@@ -255,7 +267,7 @@ def attention_with_cache(x: np.ndarray, params: Dict[str, np.ndarray], heads: in
     (:1486-1492), SDPA without mask (:1531), gate + out projection (:1680-1700).
     """
     ctx = x if context is None else context
-    f64 = lambda a: np.asarray(a, dtype=np.float64)
+    f64 = lambda a: np.asarray(a, dtype=dtype)
     q = f64(x) @ f64(params["to_q_w"]).T + f64(params["to_q_b"])
     k = f64(ctx) @ f64(params["to_k_w"]).T + f64(params["to_k_b"])
     v = f64(ctx) @ f64(params["to_v_w"]).T + f64(params["to_v_b"])
@@ -273,7 +285,7 @@ def attention_with_cache(x: np.ndarray, params: Dict[str, np.ndarray], heads: in
         v = v[:new_kv_real_len]
     full_k = k if cached_k is None else np.concatenate([f64(cached_k), k], axis=0)
     full_v = v if cached_v is None else np.concatenate([f64(cached_v), v], axis=0)
-    out = attention(q, full_k, full_v)
+    out = attention(q, full_k, full_v, dtype=dtype)
     out = out.reshape(out.shape[0], heads * dim_head)
     if "to_gate_logits_w" in params:
         g = f64(x) @ f64(params["to_gate_logits_w"]).T + f64(params["to_gate_logits_b"])

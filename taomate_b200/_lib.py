@@ -122,6 +122,14 @@ def check(status: int, what: str) -> None:
     raise TMError(text)
 
 
+LAUNCHES = 0  # kernel launches issued through this binding (for launch accounting)
+
+
+def launched(n: int = 1) -> None:
+    global LAUNCHES
+    LAUNCHES += n
+
+
 def stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 

@@ -26,6 +26,7 @@ from torch import Tensor
 from . import _lib
 from . import parallel as P
 from .kv_cache import ArenaKV, cache_rows_view
+from .profiler import section
 from .rope import norm_rope
 
 
@@ -85,6 +86,7 @@ def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tens
             new_v.data_ptr() if new_v is not None else None, nbs, nrs, nrows,
             arr, len(spans), out.data_ptr(), obs, ors, B, Lq, H, D,
             float(scale) if scale is not None else 0.0, _lib.stream_ptr(dev)), "attention")
+        _lib.launched()
     return out
 
 
@@ -158,10 +160,12 @@ def attention_with_cache(
     if abs(eps_q - eps_k) > 0:
         raise NotImplementedError("q_norm and k_norm with different eps")
 
+    base = profile_name or ("self" if context is None else "cross")
     # 2-3. fused norm + RoPE (+ send layout) and the seq->head exchange
     if sp_size == 1:
-        q, k = norm_rope([q, k], [attn.q_norm.weight, attn.k_norm.weight], [q_pe, kk_pe], H, D,
-                         eps_q)
+        with section(base + ".rope_reshape"):
+            q, k = norm_rope([q, k], [attn.q_norm.weight, attn.k_norm.weight], [q_pe, kk_pe], H,
+                             D, eps_q)
         v = v.view(B, -1, H, D)
         if logit_log_scale is not None:
             s = logit_log_scale.to(q.dtype)
@@ -169,9 +173,11 @@ def attention_with_cache(
     else:
         same = (q.shape == k.shape == v.shape)
         if same:
-            send = norm_rope([q, k, v], [attn.q_norm.weight, attn.k_norm.weight, None],
-                             [q_pe, kk_pe, None], H, D, eps_q, sp_size=sp_size, packed=True)
-            q, k, v = P.seq_all_to_all_head_packed(send, P.get_sp_group(), sp_size)
+            with section(base + ".rope_reshape"):
+                send = norm_rope([q, k, v], [attn.q_norm.weight, attn.k_norm.weight, None],
+                                 [q_pe, kk_pe, None], H, D, eps_q, sp_size=sp_size, packed=True)
+            with section(base + ".a2a_seq2head"):
+                q, k, v = P.seq_all_to_all_head_packed(send, P.get_sp_group(), sp_size)
         else:
             sq, sk, sv = norm_rope([q, k, v], [attn.q_norm.weight, attn.k_norm.weight, None],
                                    [q_pe, kk_pe, None], H, D, eps_q, sp_size=sp_size)
@@ -195,11 +201,13 @@ def attention_with_cache(
     ck, cv, spans = _cache_source(cached_k, cached_v)
     if q.stride(3) != 1 or q.stride(2) != D:
         q = q.contiguous()
-    out = flash_attention(q, ck, cv, spans, k, v, nk_rows)
+    with section(base + ".sdpa"):
+        out = flash_attention(q, ck, cv, spans, k, v, nk_rows)
 
     # 5. head -> seq
     if sp_size > 1:
-        out = P.head_all_to_all_seq(out, P.get_sp_group(), sp_size)
+        with section(base + ".a2a_head2seq"):
+            out = P.head_all_to_all_seq(out, P.get_sp_group(), sp_size)
 
     # 6. gate + out projection (kv_cache.py:1680-1700)
     out = out.reshape(B, -1, H * D)
@@ -208,3 +216,35 @@ def attention_with_cache(
         out = (out.view(B, -1, H, D) * gates.unsqueeze(-1)).view(B, -1, H * D)
     out = attn.to_out(out)
     return out, k, v
+
+
+class AttentionWeights(torch.nn.Module):
+    """Weight container with the attribute names of the reference's
+    ``CausalLTXAttention`` (ltx_causal/attention/causal_attention.py:55-118):
+    ``to_q/to_k/to_v`` (bias), ``q_norm/k_norm`` (RMSNorm over heads*dim_head),
+    ``to_out[0]`` and optional ``to_gate_logits``.  For benchmarks and tests
+    on machines without the reference package; ``attention_with_cache`` takes
+    either."""
+
+    def __init__(self, query_dim: int, heads: int, dim_head: int, context_dim: Optional[int] = None,
+                 norm_eps: float = 1e-6, gated: bool = False, device=None,
+                 dtype: torch.dtype = torch.bfloat16, std: Optional[float] = 0.02):
+        super().__init__()
+        inner = heads * dim_head
+        ctx = query_dim if context_dim is None else context_dim
+        kw = dict(device=device, dtype=dtype)
+        self.heads, self.dim_head, self.inner_dim = heads, dim_head, inner
+        self.to_q = torch.nn.Linear(query_dim, inner, bias=True, **kw)
+        self.to_k = torch.nn.Linear(ctx, inner, bias=True, **kw)
+        self.to_v = torch.nn.Linear(ctx, inner, bias=True, **kw)
+        self.q_norm = torch.nn.RMSNorm(inner, eps=norm_eps, **kw)
+        self.k_norm = torch.nn.RMSNorm(inner, eps=norm_eps, **kw)
+        self.to_gate_logits = torch.nn.Linear(query_dim, heads, bias=True, **kw) if gated else None
+        self.to_out = torch.nn.Sequential(torch.nn.Linear(inner, query_dim, bias=True, **kw),
+                                          torch.nn.Identity())
+        if std is not None:
+            with torch.no_grad():
+                for m in self.modules():
+                    if isinstance(m, torch.nn.Linear):
+                        m.weight.normal_(0.0, std)
+                        m.bias.normal_(0.0, std)

@@ -91,6 +91,7 @@ def _slice_tensor(tensor: torch.Tensor, spans: List[Tuple[int, int]]) -> torch.T
     with torch.cuda.device(dev):
         _lib.check(_lib.load().tm_copy_rows(spans_c, i, row_bytes, _lib.stream_ptr(dev)),
                    "_slice_tensor")
+        _lib.launched()
     return out
 
 

@@ -117,6 +117,7 @@ class KVArena:
         with torch.cuda.device(dev):
             _lib.check(_lib.load().tm_copy_rows(spans, i, row_bytes, _lib.stream_ptr(dev)),
                        "KVArena.write")
+            _lib.launched()
         self.appends += 1
         return entries
 
@@ -185,6 +186,7 @@ class ArenaKV:
         with torch.cuda.device(dev):
             _lib.check(_lib.load().tm_copy_rows(spans, i, row_bytes, _lib.stream_ptr(dev)),
                        "ArenaKV.materialize")
+            _lib.launched()
         return out
 
     def __repr__(self) -> str:
@@ -344,6 +346,7 @@ def cat_tensors(a: Tensor, b: Tensor) -> Tensor:
         with torch.cuda.device(dev):
             _lib.check(_lib.load().tm_copy_rows(spans, i, row_bytes, _lib.stream_ptr(dev)),
                        "cat_tensors")
+            _lib.launched()
     return out
 
 

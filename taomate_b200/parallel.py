@@ -139,6 +139,7 @@ def permute_copy(x: torch.Tensor, perm: Sequence[int]) -> torch.Tensor:
         _lib.check(_lib.load().tm_strided_copy5(xp.data_ptr(), out.data_ptr(), sizes, sst, dst,
                                                 x.element_size(), _lib.stream_ptr(x.device)),
                    "permute_copy")
+        _lib.launched()
     return out
 
 

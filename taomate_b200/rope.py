@@ -119,6 +119,7 @@ def causal_precompute_freqs_cis(
                                                 mp, int(start_frame), int(bool(is_audio)),
                                                 int(repeat_per_frame), stream),
                        "causal_precompute_freqs_cis")
+            _lib.launched()
     return cos, sin
 
 
@@ -201,6 +202,7 @@ def norm_rope(xs, weights, pes, heads: int, dim_head: int, eps: float, sp_size: 
     with torch.cuda.device(dev):
         _lib.check(lib.tm_norm_rope(jobs, n, B, int(heads), int(dim_head), float(eps),
                                     int(sp_size), _lib.stream_ptr(dev)), "norm_rope")
+        _lib.launched()
     return buf if packed else outs
 
 
