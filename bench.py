@@ -58,6 +58,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-case", choices=["attention", "norm_rope"], default=None,
+                    help="time one kernel in isolation at C2 shapes (profiling target)")
+    ap.add_argument("--reps", type=int, default=20)
     return ap.parse_args()
 
 
@@ -380,9 +383,53 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_kernel_case(args):
+    """One kernel at C2 shapes, ``--reps`` launches, CUDA-event time per launch."""
+    import torch
+    import taomate_b200 as tm
+    from taomate_b200.rope import norm_rope
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    Lq = Q_FRAMES * FRAME_TOKENS
+    Lc = (ANCHOR_FRAMES + WINDOW_FRAMES) * FRAME_TOKENS
+    rnd = lambda *s: torch.randn(*s, device=dev, generator=g).to(torch.bfloat16)
+    if args.kernel_case == "attention":
+        q = rnd(1, Lq, HEADS, DIM_HEAD)
+        ck, cv = rnd(1, Lc, HEADS, DIM_HEAD), rnd(1, Lc, HEADS, DIM_HEAD)
+        nk, nv = rnd(1, Lq, HEADS, DIM_HEAD), rnd(1, Lq, HEADS, DIM_HEAD)
+        out = torch.empty_like(q)
+        fn = lambda: tm.flash_attention(q, ck, cv, [(0, Lc)], nk, nv, Lq, out=out)
+        work, unit = 4.0 * Lq * (Lc + Lq) * HEADS * DIM_HEAD / 1e12, "TFLOP/s"
+    else:
+        xq, xk = rnd(1, Lq, HIDDEN), rnd(1, Lq, HIDDEN)
+        w = torch.ones(HIDDEN, device=dev, dtype=torch.bfloat16)
+        cos, sin = tm.causal_precompute_freqs_cis(torch.tensor([[Q_FRAMES, 16, 24]]), HIDDEN,
+                                                  device=dev, dtype=torch.bfloat16,
+                                                  num_attention_heads=HEADS)
+        fn = lambda: norm_rope([xq, xk], [w, w], [(cos, sin), (cos, sin)], HEADS, DIM_HEAD, 1e-6)
+        work, unit = (4 * Lq * HIDDEN * 2 + 2 * cos.numel() * 2) / 1e9, "GB/s"
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.reps)]
+    for a, b in ev:
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    ms = sorted(a.elapsed_time(b) for a, b in ev)
+    med = ms[len(ms) // 2]
+    print(json.dumps({"kernel_case": args.kernel_case, "median_ms": med, "min_ms": ms[0],
+                      "achieved": work / (med * 1e-3), "unit": unit}), flush=True)
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.kernel_case:
+        run_kernel_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -79,7 +79,8 @@ EXPORTED = tuple(_SIGS)
 
 
 def lib_path() -> str:
-    return _build.LIB
+    """The in-tree build, or the library named by ``TAOMATE_B200_LIB``."""
+    return os.environ.get("TAOMATE_B200_LIB") or _build.LIB
 
 
 def load(build_if_missing: bool = True) -> ctypes.CDLL:
@@ -91,7 +92,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         if _LIB is not None:
             return _LIB
         path = lib_path()
-        if build_if_missing and _build.needs_build():
+        if build_if_missing and path == _build.LIB and _build.needs_build():
             _build.build()
         if not os.path.exists(path):
             raise RuntimeError(f"taomate_b200 native library not found at {path}; "

@@ -6,10 +6,13 @@ Tolerances:
   two libraries differ by an ulp (< 0.5 % of entries).
 * norm + RoPE on identical bf16 inputs: relative L2 <= 2e-3 against the fp32
   oracle.
-* attention on identical bf16 inputs: relative L2 <= 2e-3 against the
-  reference's own GPU path (torch SDPA in bf16), and no further from the
-  fp32 result than that path is (x1.1).  Rounding the exact fp32 result to
-  bf16 alone costs ~1.7e-3, so 2e-3 against fp32 is below the bf16 floor.
+* attention on identical bf16 inputs: no further from the exact (fp32)
+  result than the reference's own GPU path (torch SDPA in bf16) is, and
+  within 4e-3 of that path's output.  Both round P and the output to bf16;
+  rounding the exact result to bf16 alone costs ~1.7e-3, and the two
+  kernels round P at different running maxima (this kernel splits the keys
+  between two softmax warpgroups), so their outputs differ by ~2.5e-3 while
+  each is ~2.34e-3 from exact.
 * ``attention_with_cache`` end to end (bf16 projections included): no worse
   than 1.25x the reference's own bf16 path, both measured against the
   reference's fp32 output on the same inputs.
@@ -179,8 +182,8 @@ def assert_attention_parity(out, q, ks, vs, scale=None):
     ref = _sdpa_ref(q, ks, vs, scale)
     refb = _sdpa_bf16(q, ks, vs, scale)
     assert torch.isfinite(out).all()
-    assert rel_l2(out, refb) < 2e-3
-    assert rel_l2(out, ref) < 1.1 * rel_l2(refb, ref) + 1e-4
+    assert rel_l2(out, ref) < 1.02 * rel_l2(refb, ref) + 1e-4
+    assert rel_l2(out, refb) < 4e-3
 
 
 ATTN_SHAPES = [
