@@ -86,7 +86,7 @@ TM_API int tm_rope_tables_split(void* cos_out, void* sin_out, int out_dtype, int
  *   cos/sin: [B, H, L, D/2] bf16 with the given strides, or NULL for no RoPE
  *   (a job with neither is a pure layout copy, used for V).
  * Up to 4 jobs (q, k, v) run in one launch.  D in {64, 128};
- * H*D a multiple of 256 and at most 4096.  Rows must be 16-byte aligned.
+ * H*D in {256, 512, 1024, 2048, 4096}.  Rows must be 16-byte aligned.
  */
 typedef struct {
   const void* x;

@@ -98,10 +98,12 @@ __global__ void tables_kernel(const TableParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// A2 + A3: one warp per token row.  The row (H*D bf16) is read in 16-byte
-// chunks, chunk c = k*32 + lane, so every load instruction of the warp covers
-// 512 contiguous bytes.  Within a head of D/8 chunks, rotate-half pairs chunk j
-// with chunk j +- D/16, which sits in lane ^ (D/16) at the same k.
+// A2 + A3: one block of TPR = H*D / (8 * CPT) threads per token row; thread t
+// handles the 16-byte chunks c = k * TPR + t (k < CPT), so every load
+// instruction of a warp covers 512 contiguous bytes and all of a thread's loads
+// (x, weight, cos, sin) are independent and issued up front.  Within a head of
+// D/8 chunks, rotate-half pairs chunk j with chunk j +- D/16, held by thread
+// t ^ (D/16) of the same warp.  The sum of squares is reduced over the block.
 // ---------------------------------------------------------------------------
 constexpr int kMaxJobs = 4;
 
@@ -133,67 +135,88 @@ __device__ __forceinline__ void unpack8(const uint4& v, float* f) {
   }
 }
 
-template <int D, int CPL>
-__global__ void __launch_bounds__(256) norm_rope_kernel(const __grid_constant__ NormRopeParams p) {
+template <int D, int CPT, int TPR>
+__global__ void __launch_bounds__(TPR) norm_rope_kernel(const __grid_constant__ NormRopeParams p) {
   constexpr int kChunksPerHead = D / 8;
   constexpr int kHalf = D / 16;
-  constexpr int kInner = CPL * 32 * 8;
-  const int lane = threadIdx.x & 31;
-  const int64_t gw = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
-  if (gw >= p.row_begin[p.n_jobs]) return;
+  constexpr int kInner = CPT * TPR * 8;
+  constexpr int kWarps = TPR / 32;
+  __shared__ float red[kWarps];
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const int64_t row = blockIdx.x;
   int ji = 0;
 #pragma unroll
   for (int i = 1; i < kMaxJobs; ++i)
-    if (i < p.n_jobs && gw >= p.row_begin[i]) ji = i;
+    if (i < p.n_jobs && row >= p.row_begin[i]) ji = i;
   const Job& jb = p.jobs[ji];
-  const int64_t r = gw - p.row_begin[ji];
+  const int64_t r = row - p.row_begin[ji];
   const int64_t b = r / jb.L;
   const int64_t l = r % jb.L;
+  const int j = t % kChunksPerHead;  // chunk position within its head (same for every k)
+  const bool first_half = j < kHalf;
 
   const __nv_bfloat16* xrow = jb.x + b * jb.xbs + l * jb.xrs;
-  float y[CPL][8];
-  float ss = 0.f;
+  uint4 xr[CPT], cr[CPT], sr[CPT], wr[CPT];
 #pragma unroll
-  for (int k = 0; k < CPL; ++k) {
-    const uint4 v = *reinterpret_cast<const uint4*>(xrow + (k * 32 + lane) * 8);
-    unpack8(v, y[k]);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) ss = fmaf(y[k][i], y[k][i], ss);
-  }
-  if (jb.w != nullptr) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float rs = rsqrtf(ss / static_cast<float>(kInner) + p.eps);
-#pragma unroll
-    for (int k = 0; k < CPL; ++k) {
-      float w[8];
-      unpack8(*reinterpret_cast<const uint4*>(jb.w + (k * 32 + lane) * 8), w);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) y[k][i] = y[k][i] * rs * w[i];
+  for (int k = 0; k < CPT; ++k) {
+    const int c = k * TPR + t;
+    xr[k] = *reinterpret_cast<const uint4*>(xrow + c * 8);
+    if (jb.w != nullptr) wr[k] = __ldg(reinterpret_cast<const uint4*>(jb.w + c * 8));
+    if (jb.cos != nullptr) {
+      const int h = c / kChunksPerHead;
+      const int64_t pe_off = b * jb.pbs + h * jb.phs + l * jb.prs + (j % kHalf) * 8;
+      cr[k] = *reinterpret_cast<const uint4*>(jb.cos + pe_off);
+      sr[k] = *reinterpret_cast<const uint4*>(jb.sin + pe_off);
     }
   }
-  const int j = lane % kChunksPerHead;
-  const bool first_half = j < kHalf;
+  float rs = 1.0f;
+  if (jb.w != nullptr) {
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < CPT; ++k) {
+      float f[8];
+      unpack8(xr[k], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (kWarps > 1) {
+      if (lane == 0) red[t >> 5] = ss;
+      __syncthreads();
+      ss = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) ss += red[w];
+    }
+    rs = rsqrtf(ss / static_cast<float>(kInner) + p.eps);
+  }
   const int Hl = p.H / p.sp;
 #pragma unroll
-  for (int k = 0; k < CPL; ++k) {
-    const int c = k * 32 + lane;
+  for (int k = 0; k < CPT; ++k) {
+    const int c = k * TPR + t;
     const int h = c / kChunksPerHead;
+    float y[8];
+    unpack8(xr[k], y);
+    if (jb.w != nullptr) {
+      float w[8];
+      unpack8(wr[k], w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = y[i] * rs * w[i];
+    }
     float o[8];
     if (jb.cos != nullptr) {
       float cs[8], sn[8], part[8];
-      const int64_t pe_off = b * jb.pbs + h * jb.phs + l * jb.prs + (j % kHalf) * 8;
-      unpack8(*reinterpret_cast<const uint4*>(jb.cos + pe_off), cs);
-      unpack8(*reinterpret_cast<const uint4*>(jb.sin + pe_off), sn);
+      unpack8(cr[k], cs);
+      unpack8(sr[k], sn);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) part[i] = __shfl_xor_sync(0xffffffffu, y[k][i], kHalf);
+      for (int i = 0; i < 8; ++i) part[i] = __shfl_xor_sync(0xffffffffu, y[i], kHalf);
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        o[i] = first_half ? fmaf(y[k][i], cs[i], -part[i] * sn[i])
-                          : fmaf(y[k][i], cs[i], part[i] * sn[i]);
+        o[i] = first_half ? fmaf(y[i], cs[i], -part[i] * sn[i]) : fmaf(y[i], cs[i], part[i] * sn[i]);
     } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = y[k][i];
+      for (int i = 0; i < 8; ++i) o[i] = y[i];
     }
     const uint4 v = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
                                pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
@@ -204,11 +227,10 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(const __grid_constant__ 
   }
 }
 
-template <int D, int CPL>
+template <int D, int CPT, int TPR>
 static int launch_norm_rope(const NormRopeParams& prm, cudaStream_t s) {
   const int64_t rows = prm.row_begin[prm.n_jobs];
-  const int64_t blocks = (rows + 7) / 8;
-  norm_rope_kernel<D, CPL><<<static_cast<unsigned>(blocks), 256, 0, s>>>(prm);
+  norm_rope_kernel<D, CPT, TPR><<<static_cast<unsigned>(rows), TPR, 0, s>>>(prm);
   return check_cuda(cudaGetLastError(), "norm_rope: launch");
 }
 
@@ -270,9 +292,10 @@ extern "C" int tm_norm_rope(const tm_norm_rope_job* jobs, int n_jobs, int B, int
     return set_error(TM_ERR_INVALID_ARGUMENT, "norm_rope: %d jobs (1..%d)", n_jobs, kMaxJobs);
   if (D != 64 && D != 128) return set_error(TM_ERR_UNSUPPORTED, "norm_rope: head dim %d", D);
   const int inner = H * D;
-  if (B < 1 || H < 1 || inner % 256 != 0 || inner > 4096)
+  if (B < 1 || H < 1 || (inner != 256 && inner != 512 && inner != 1024 && inner != 2048 &&
+                         inner != 4096))
     return set_error(TM_ERR_INVALID_ARGUMENT,
-                     "norm_rope: H*D=%d must be a positive multiple of 256 up to 4096", inner);
+                     "norm_rope: H*D=%d must be 256, 512, 1024, 2048 or 4096", inner);
   if (sp_size < 1 || H % sp_size != 0)
     return set_error(TM_ERR_INVALID_ARGUMENT, "norm_rope: H (%d) must be divisible by sp_size (%d)",
                      H, sp_size);
@@ -323,23 +346,13 @@ extern "C" int tm_norm_rope(const tm_norm_rope_job* jobs, int n_jobs, int B, int
   }
   p.row_begin[n_jobs] = acc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int cpl = inner / 256;
-  if (D == 128) {
-    switch (cpl) {
-      case 2: return launch_norm_rope<128, 2>(p, s);
-      case 4: return launch_norm_rope<128, 4>(p, s);
-      case 8: return launch_norm_rope<128, 8>(p, s);
-      case 16: return launch_norm_rope<128, 16>(p, s);
-      default: break;
-    }
-  } else {
-    switch (cpl) {
-      case 1: return launch_norm_rope<64, 1>(p, s);
-      case 2: return launch_norm_rope<64, 2>(p, s);
-      case 4: return launch_norm_rope<64, 4>(p, s);
-      case 8: return launch_norm_rope<64, 8>(p, s);
-      default: break;
-    }
+  switch (inner) {  // chunks per thread x threads per row = inner / 8
+    case 256: return D == 128 ? launch_norm_rope<128, 1, 32>(p, s) : launch_norm_rope<64, 1, 32>(p, s);
+    case 512: return D == 128 ? launch_norm_rope<128, 2, 32>(p, s) : launch_norm_rope<64, 2, 32>(p, s);
+    case 1024: return D == 128 ? launch_norm_rope<128, 4, 32>(p, s) : launch_norm_rope<64, 4, 32>(p, s);
+    case 2048: return D == 128 ? launch_norm_rope<128, 4, 64>(p, s) : launch_norm_rope<64, 4, 64>(p, s);
+    case 4096: return D == 128 ? launch_norm_rope<128, 4, 128>(p, s) : launch_norm_rope<64, 4, 128>(p, s);
+    default: break;
   }
   return set_error(TM_ERR_UNSUPPORTED, "norm_rope: H*D=%d not built", inner);
 }
