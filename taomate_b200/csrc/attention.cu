@@ -1,30 +1,43 @@
 // Block-causal streaming attention on sm_100a tensor cores.
 //
-// One CTA computes a 128-row query tile of one (batch, head) against the
-// ordered list of visible key tiles (anchor + rolling window from the slot
-// arena, then the current chunk).  The key tiles are split between two
-// softmax warpgroups ("lanes"): lane 0 takes the first ceil(n/2) tiles, lane
-// 1 the rest, and the two partial results are merged at the end, so the
-// tensor core works on one lane's QK^T / PV while the other lane runs its
-// softmax.  Warp roles (12 warps, 3 warpgroups):
-//   warp 0      TMA producer: Q once, then K and V tiles (lane-interleaved
-//               order) into separate rings; K runs one tile ahead of V.
-//   warp 1      TMEM owner and tcgen05.mma issuer (one thread):
-//               S_l = Q K^T into lane l's TMEM tile, O_l += P_l V with P_l read
-//               from TMEM (TS form).
-//   warps 2..3  idle (they hand their registers to the softmax warpgroups).
-//   warps 4..7  lane 0 softmax, warps 8..11 lane 1 softmax: thread r of a
-//               warpgroup owns query row r (its TMEM lane); it reads its S row,
-//               keeps the running max / sum in registers, writes P (bf16) back
-//               over S in TMEM, and rescales O_l in TMEM only when the running
-//               max grows by more than 2^8 (the final division uses the same
-//               reference max, so the result is exact).
-//   lane 0 then merges lane 1's (O, max, sum) and writes O / sum as bf16.
+// Each CTA runs two softmax warpgroups ("lanes") over the ordered list of
+// visible 64-key tiles (anchor + rolling window from the slot arena, then the
+// current chunk) of one (batch, head):
+//   pair CTA:  lane l owns query tile 2c + l; both lanes consume every K/V tile,
+//              so a tile is loaded once for 256 query rows.
+//   split CTA: the odd last query tile of a head; both lanes use the same Q,
+//              lane 0 takes the first ceil(n/2) key tiles and lane 1 the rest,
+//              and lane 0 merges the two partial results.  Split CTAs come
+//              after the pair CTAs in grid order, so they fill the tail of the
+//              wave.
 //
-// TMEM: S0/P0 [0,128), S1/P1 [128,256), O0 [256,256+D), O1 [256+D,256+2D).
+// Shared memory: the query tile(s) (TMA, 128-byte swizzle), a 4-stage K ring
+// and a 5-stage V ring of 64-key tiles.  TMEM (512 columns): S_l at 64 l
+// (fp32), P_l double-buffered at 128 + 64 l + 32 b (bf16 pairs), O_l at
+// 256 + D l.  S_l = Q_l K^T takes both operands from shared memory; O_l += P_l V
+// takes P from TMEM.
+//
+// Warp roles (12 warps):
+//   warp 0      TMA producer of Q and of the K ring (no multicast).
+//   warp 2      TMA producer of the V ring.
+//   warp 1 / 3  tcgen05.mma issuers of lane 0 / lane 1, one thread each: a
+//               single thread issues at most one MMA every ~50 cycles, so a
+//               64-wide MMA (32 cycles of tensor work) needs two issuers to
+//               keep the tensor core busy.  Per lane the order is QK(j),
+//               PV(j - 1), QK(j + 1), ...: QK(j + 1) only needs softmax to
+//               have read S(j), so it overlaps softmax(j) and PV(j).
+//   warps 4..7  lane 0, warps 8..11 lane 1: thread r owns query row r (its TMEM
+//               lane); reads its S row, keeps running max / sum in registers,
+//               writes P (bf16) into TMEM, rescales O only when its running
+//               max grows by more than 2^8 (the final division uses the same
+//               reference max).  A fixed share of the exponentials runs on the
+//               FMA pipe (Cody-Waite split 2^x = 2^round(x) * 2^f, |f| <= 1/2,
+//               degree-3 minimax polynomial for 2^f, max relative error
+//               7.5e-5).
+//
 // Visibility (anchor + window + chunk) arrives as a host-built list of key
-// tiles, each (source, first row, valid rows); keys beyond `valid` are masked
-// to -inf in registers, nothing is materialised.
+// tiles (source, first row, valid rows); keys beyond `valid` are masked to
+// -inf in registers, nothing is materialised.
 //
 // Reference semantics: softmax(Q K^T / sqrt(D)) V without a mask over
 // cat(cached, new) (ltx_causal/transformer/kv_cache.py:1486-1531,
@@ -38,15 +51,17 @@
 namespace tmb {
 namespace attn {
 
-constexpr int BM = 128;          // query rows per CTA (one TMEM lane each)
-constexpr int BN = 128;          // keys per tile
-constexpr int kMaxTiles = 192;   // 24576 visible keys
+constexpr int BM = 128;          // query rows per lane (one TMEM lane each)
+constexpr int BN = 64;           // keys per tile
+constexpr int kMaxTiles = 384;   // 24576 visible keys
 constexpr int kThreads = 384;    // 12 warps
 // Register split (setmaxnreg): launched at 168 per thread (384 x 168 =
 // 64512); warpgroup 0 drops to 88, the two softmax warpgroups rise to 208:
 // 128 x 88 + 256 x 208 = 64512, the launch total.
 constexpr int kRegsCtrl = 88;
 constexpr int kRegsSoftmax = 208;
+// Exponentials on the FMA pipe: kEmulPairs of every 4 column pairs.
+constexpr int kEmulPairs = 1;
 
 struct __align__(64) Params {
   CUtensorMap tm_q;
@@ -54,6 +69,7 @@ struct __align__(64) Params {
   CUtensorMap tm_v[2];
   int2 tiles[kMaxTiles];  // x = (source << 30) | first row, y = valid rows (1..BN)
   int n_tiles;
+  int n_qtiles;            // ceil(Lq / BM)
   int Lq;
   int64_t out_bs, out_rs;  // elements
   __nv_bfloat16* out;
@@ -63,25 +79,53 @@ struct __align__(64) Params {
 
 template <int D>
 struct Cfg {
-  static constexpr int kKStages = 3;
-  static constexpr int kVStages = (D == 128) ? 2 : 3;
-  static constexpr int kBlk = 128 * 128;  // bytes of one 128-row x 64-col swizzle block
+  static constexpr int kKStages = 4;
+  static constexpr int kVStages = 5;
+  static constexpr int kBlk = BN * 128;   // one 64-key x 64-column swizzle block of K / V
+  static constexpr int kQBlk = BM * 128;  // one 128-row x 64-column block of Q
   static constexpr int kQBytes = BM * D * 2;
   static constexpr int kKVBytes = BN * D * 2;
   static constexpr int kQOff = 0;
-  static constexpr int kKOff = kQOff + kQBytes;
+  static constexpr int kKOff = kQOff + 2 * kQBytes;
   static constexpr int kVOff = kKOff + kKStages * kKVBytes;
   static constexpr int kBarOff = kVOff + kVStages * kKVBytes;
   // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
-  //           s_full[2], p_full[2], pv_done[2], drain
-  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 6 + 1;
+  //           s_full[2], s_free[2], p_full[2][2], pv_done[2][2], drain[2]
+  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 14;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
   static constexpr int kMLOff = kMiscOff + 16;             // lane-1 max / sum per row
   static constexpr int kSmemBytes = kMLOff + 2 * BM * 4;
   static constexpr int kSmemAlloc = kSmemBytes + 1024;     // runtime 1 KB alignment slack
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kOCol = 256;                   // O_l at kOCol + l * D
+  static constexpr uint32_t kSCol = 0;     // S_l at kSCol + 64 l
+  static constexpr uint32_t kPCol = 128;   // P_l,b at kPCol + 64 l + 32 b
+  static constexpr uint32_t kOCol = 256;   // O_l at kOCol + D l
 };
+
+// 2^x on the FMA / ALU pipes for two values: x clamped to >= -126, split as
+// round(x) + f, 2^f from a degree-3 minimax polynomial, exponent added in the
+// integer domain.
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
+  const uint64_t kMagic = f2_packf(12582912.0f, 12582912.0f);   // 1.5 * 2^23
+  const uint64_t kNegMagic = f2_packf(-12582912.0f, -12582912.0f);
+  const uint64_t kNegOne = f2_packf(-1.0f, -1.0f);
+  const uint64_t c0 = f2_packf(0.99992806f, 0.99992806f);
+  const uint64_t c1 = f2_packf(0.69326097f, 0.69326097f);
+  const uint64_t c2 = f2_packf(0.24261114f, 0.24261114f);
+  const uint64_t c3 = f2_packf(0.05517167f, 0.05517167f);
+  const uint64_t xc = f2_packf(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const uint64_t t = f2_add(xc, kMagic);      // round(x) in the low mantissa bits
+  const uint64_t r = f2_add(t, kNegMagic);    // round(x) as a float
+  const uint64_t f = f2_fma(r, kNegOne, xc);  // x - round(x), in [-0.5, 0.5]
+  uint64_t pp = f2_fma(f, c3, c2);
+  pp = f2_fma(pp, f, c1);
+  pp = f2_fma(pp, f, c0);
+  float t0, t1, p0, p1;
+  f2_unpack(t, t0, t1);
+  f2_unpack(pp, p0, p1);
+  y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ Params p) {
@@ -94,46 +138,56 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   const uint32_t sbase = smem_addr(smem);
   const int warp = threadIdx.x >> 5;
   const int lane_id = threadIdx.x & 31;
-  const int q_tile = blockIdx.x, head = blockIdx.y, batch = blockIdx.z;
+  const int head = blockIdx.x, cta = blockIdx.y, batch = blockIdx.z;
   const int n = p.n_tiles;
-  const int n0 = (n + 1) >> 1;  // lane 0 tiles [0, n0), lane 1 tiles [n0, n)
-  const int n1 = n - n0;
+  const int pairs = p.n_qtiles >> 1;
+  const bool split = cta >= pairs;  // the odd last query tile
+  const int qt0 = 2 * cta;
+  // key tiles per lane; split: lane 0 [0, n0), lane 1 [n0, n); pair: both [0, n)
+  const int n0 = split ? (n + 1) >> 1 : n;
+  const int n1 = split ? n - n0 : n;
 
   const uint32_t bar0 = sbase + C::kBarOff;
-  const uint32_t b_q = bar0;
+  const uint32_t b_qfull = bar0;
   auto b_kfull = [&](int s) { return bar0 + 8u * (1 + s); };
   auto b_kempty = [&](int s) { return bar0 + 8u * (1 + KS + s); };
   auto b_vfull = [&](int s) { return bar0 + 8u * (1 + 2 * KS + s); };
   auto b_vempty = [&](int s) { return bar0 + 8u * (1 + 2 * KS + VS + s); };
   const uint32_t bar1 = bar0 + 8u * (1 + 2 * KS + 2 * VS);
   auto b_sfull = [&](int l) { return bar1 + 8u * l; };
-  auto b_pfull = [&](int l) { return bar1 + 8u * (2 + l); };
-  auto b_pvdone = [&](int l) { return bar1 + 8u * (4 + l); };
-  const uint32_t b_drain = bar1 + 8u * 6;
+  auto b_sfree = [&](int l) { return bar1 + 8u * (2 + l); };
+  auto b_pfull = [&](int l, int b) { return bar1 + 8u * (4 + 2 * l + b); };
+  auto b_pvdone = [&](int l, int b) { return bar1 + 8u * (8 + 2 * l + b); };
+  auto b_drain = [&](int l) { return bar1 + 8u * (12 + l); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
   float* m1_smem = reinterpret_cast<float*>(smem + C::kMLOff);
   float* l1_smem = m1_smem + BM;
 
-  // item g (consumption order) -> tile: rounds of (lane 0, lane 1)
-  auto tile_of = [&](int g) { return (g & 1) ? n0 + (g >> 1) : (g >> 1); };
+  // stream item -> key tile; lane step -> stream item
+  auto tile_of = [&](int g) { return split ? ((g & 1) ? n0 + (g >> 1) : (g >> 1)) : g; };
+  auto item_of = [&](int l, int j) { return split ? 2 * j + l : j; };
 
   if (threadIdx.x == 0) {
-    mbar_init(b_q, 1);
+    const uint32_t consumers = split ? 1u : 2u;
+    mbar_init(b_qfull, 1);
     for (int s = 0; s < KS; ++s) {
       mbar_init(b_kfull(s), 1);
-      mbar_init(b_kempty(s), 1);
+      mbar_init(b_kempty(s), consumers);
     }
     for (int s = 0; s < VS; ++s) {
       mbar_init(b_vfull(s), 1);
-      mbar_init(b_vempty(s), 1);
+      mbar_init(b_vempty(s), consumers);
     }
     for (int l = 0; l < 2; ++l) {
       mbar_init(b_sfull(l), 1);
-      mbar_init(b_pfull(l), 128);
-      mbar_init(b_pvdone(l), 1);
+      mbar_init(b_sfree(l), 128);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(b_pfull(l, b), 128);
+        mbar_init(b_pvdone(l, b), 1);
+      }
+      mbar_init(b_drain(l), 1);
     }
-    mbar_init(b_drain, 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -155,20 +209,26 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 
   if (warp < 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsCtrl));
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ producer
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------------ producers
     if (lane_id == 0) {
       constexpr int kDB = D / 64;
-      mbar_arrive_expect_tx(b_q, C::kQBytes);
-      for (int db = 0; db < kDB; ++db)
-        tma_load_4d(sbase + C::kQOff + db * C::kBlk, &p.tm_q, b_q, db * 64, head, q_tile * BM,
-                    batch);
-      auto load = [&](int g, bool is_k) -> bool {
-        const int S = is_k ? KS : VS;
+      const bool is_k = warp == 0;
+      const int S = is_k ? KS : VS;
+      if (is_k) {
+        const int nq = split ? 1 : 2;
+        mbar_arrive_expect_tx(b_qfull, nq * C::kQBytes);
+        for (int t = 0; t < nq; ++t)
+          for (int db = 0; db < kDB; ++db)
+            tma_load_4d(sbase + C::kQOff + t * C::kQBytes + db * C::kQBlk, &p.tm_q, b_qfull,
+                        db * 64, head, (qt0 + t) * BM, batch);
+      }
+      int last = -1;
+      for (int g = 0; g < n; ++g) {
         const int s = g % S;
         if (g >= S && !mbar_wait(is_k ? b_kempty(s) : b_vempty(s), ((g / S) - 1) & 1, abort_flag,
                                  p.err))
-          return false;
+          break;
         const int2 tile = p.tiles[tile_of(g)];
         const int src = tile.x >> 30;
         const int row = tile.x & 0x3FFFFFFF;
@@ -178,80 +238,72 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         mbar_arrive_expect_tx(full, C::kKVBytes);
         for (int db = 0; db < kDB; ++db)
           tma_load_4d(dst + db * C::kBlk, map, full, db * 64, head, row, batch);
-        return true;
-      };
-      int last_k = -1, last_v = -1;
-      for (int g = 0; g <= n; ++g) {
-        if (g < n) {
-          if (!load(g, true)) break;
-          last_k = g;
-        }
-        if (g >= 1) {
-          if (!load(g - 1, false)) break;
-          last_v = g - 1;
-        }
+        last = g;
       }
       if (*abort_flag) {
         // Let every issued copy land before the CTA's shared memory is released.
-        mbar_wait(b_q, 0, nullptr, p.err, 100000000ull);
-        for (int g = last_k - KS + 1; g <= last_k; ++g)
-          if (g >= 0) mbar_wait(b_kfull(g % KS), (g / KS) & 1, nullptr, p.err, 100000000ull);
-        for (int g = last_v - VS + 1; g <= last_v; ++g)
-          if (g >= 0) mbar_wait(b_vfull(g % VS), (g / VS) & 1, nullptr, p.err, 100000000ull);
+        if (is_k) mbar_wait(b_qfull, 0, nullptr, p.err, 100000000ull);
+        for (int g = last - S + 1; g <= last; ++g)
+          if (g >= 0)
+            mbar_wait(is_k ? b_kfull(g % S) : b_vfull(g % S), (g / S) & 1, nullptr, p.err,
+                      100000000ull);
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane_id == 0) {
+  } else if (warp == 1 || warp == 3) {
+    // ------------------------------------------------------------------ MMA issuers
+    const int l = warp == 1 ? 0 : 1;
+    const int nl = l == 0 ? n0 : n1;
+    if (lane_id == 0 && nl > 0) {
       constexpr uint32_t idesc_qk = idesc_bf16_f32(BM, BN, 0);
       constexpr uint32_t idesc_pv = idesc_bf16_f32(BM, D, 1);
-      bool ok = mbar_wait(b_q, 0, abort_flag, p.err);
-      for (int j = 0; ok && j < n0; ++j) {
-        for (int l = 0; l < 2 && ok; ++l) {
-          const int g = 2 * j + l;
-          if (g >= n) break;
+      const int qsel = split ? 0 : l;
+      // Descriptors are built once; per tile and K-step only the start
+      // address field (bytes >> 4, low bits) moves.
+      const uint64_t qd = smem_desc_sw128(sbase + C::kQOff + qsel * C::kQBytes, 16, 1024);
+      const uint64_t kd0 = smem_desc_sw128(sbase + C::kKOff, 16, 1024);
+      const uint64_t vd0 = smem_desc_sw128(sbase + C::kVOff, C::kBlk, 1024);
+      const uint32_t tS = tmem + C::kSCol + l * BN;
+      const uint32_t tP = tmem + C::kPCol + l * 64;
+      const uint32_t tO = tmem + C::kOCol + l * D;
+      bool ok = mbar_wait(b_qfull, 0, abort_flag, p.err);
+      for (int j = 0; ok && j <= nl; ++j) {
+        if (j < nl) {
+          const int g = item_of(l, j);
           const int s = g % KS;
           if (!mbar_wait(b_kfull(s), (g / KS) & 1, abort_flag, p.err)) { ok = false; break; }
-          // S_l / P_l is free once PV_l(j - 1) has completed.
-          if (j >= 1 && !mbar_wait(b_pvdone(l), (j - 1) & 1, abort_flag, p.err)) {
-            ok = false;
-            break;
-          }
+          if (j > 0 && !mbar_wait(b_sfree(l), (j - 1) & 1, abort_flag, p.err)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t kbase = sbase + C::kKOff + s * C::kKVBytes;
+          const uint64_t kd = kd0 + static_cast<uint64_t>(s * (C::kKVBytes >> 4));
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint64_t a =
-                smem_desc_sw128(sbase + C::kQOff + (kk >> 2) * C::kBlk + (kk & 3) * 32, 16, 1024);
-            const uint64_t b =
-                smem_desc_sw128(kbase + (kk >> 2) * C::kBlk + (kk & 3) * 32, 16, 1024);
-            umma_ss(tmem + l * BN, a, b, idesc_qk, kk > 0 ? 1u : 0u);
+            const uint32_t qo = ((kk >> 2) * C::kQBlk + (kk & 3) * 32) >> 4;
+            const uint32_t ko = ((kk >> 2) * C::kBlk + (kk & 3) * 32) >> 4;
+            umma_ss(tS, qd + qo, kd + ko, idesc_qk, kk > 0 ? 1u : 0u);
           }
           umma_commit(b_sfull(l));
           umma_commit(b_kempty(s));
         }
-        for (int l = 0; l < 2 && ok; ++l) {
-          const int g = 2 * j + l;
-          if (g >= n) break;
-          const int sv = g % VS;
-          if (!mbar_wait(b_pfull(l), j & 1, abort_flag, p.err)) { ok = false; break; }
-          if (!mbar_wait(b_vfull(sv), (g / VS) & 1, abort_flag, p.err)) { ok = false; break; }
+        if (j > 0) {
+          const int jp = j - 1;
+          const int g = item_of(l, jp);
+          const int s = g % VS;
+          const int b = jp & 1;
+          if (!mbar_wait(b_pfull(l, b), (jp >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
+          if (!mbar_wait(b_vfull(s), (g / VS) & 1, abort_flag, p.err)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t vbase = sbase + C::kVOff + sv * C::kKVBytes;
+          const uint64_t vd = vd0 + static_cast<uint64_t>(s * (C::kKVBytes >> 4));
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint64_t b = smem_desc_sw128(vbase + kk * 2048, C::kBlk, 1024);
-            umma_ts(tmem + C::kOCol + l * D, tmem + l * BN + kk * 8, b, idesc_pv,
-                    (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(b_pvdone(l));
-          umma_commit(b_vempty(sv));
+          for (int kk = 0; kk < BN / 16; ++kk)
+            umma_ts(tO, tP + b * 32 + kk * 8, vd + static_cast<uint64_t>(kk * (2048 >> 4)),
+                    idesc_pv, (jp > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(b_pvdone(l, b));
+          umma_commit(b_vempty(s));
         }
       }
       if (!ok) {
-        // Drain: wait for every issued MMA before TMEM is released.
-        umma_commit(b_drain);
-        mbar_wait(b_drain, 0, nullptr, p.err, 100000000ull);
+        // Drain: wait for every MMA this thread issued before TMEM is released.
+        umma_commit(b_drain(l));
+        mbar_wait(b_drain(l), 0, nullptr, p.err, 100000000ull);
       }
     }
   } else if (warp >= 4) {
@@ -261,10 +313,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane_id;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
-    const uint32_t tS = t_lane + ln * BN;
+    const uint32_t tS = t_lane + C::kSCol + ln * BN;
+    const uint32_t tP = t_lane + C::kPCol + ln * 64;
     const uint32_t tO = t_lane + C::kOCol + ln * D;
     const int my_n = ln == 0 ? n0 : n1;
-    const int tile0 = ln == 0 ? 0 : n0;
+    const int tile0 = (split && ln == 1) ? n0 : 0;
+    const int qi = (split ? qt0 : qt0 + ln) * BM + row;
     const float sl = p.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
@@ -272,15 +326,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       bool w = mbar_wait(bar, par, abort_flag, p.err);
       return __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
     };
+    const uint64_t sl2 = f2_packf(sl, sl);
     for (int j = 0; j < my_n; ++j) {
       if (!wait_all(b_sfull(ln), j & 1)) { ok = false; break; }
       tc_fence_after();
       uint32_t sr[BN];
       TM_TMEM_LD32(tS + 0, (sr + 0));
       TM_TMEM_LD32(tS + 32, (sr + 32));
-      TM_TMEM_LD32(tS + 64, (sr + 64));
-      TM_TMEM_LD32(tS + 96, (sr + 96));
       tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(b_sfree(ln));  // S_l may now be overwritten by QK(j + 1)
 
       const int valid = p.tiles[tile0 + j].y;
       if (valid < BN) {
@@ -288,107 +343,126 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         for (int c = 0; c < BN; ++c)
           if (c >= valid) sr[c] = __float_as_uint(-INFINITY);
       }
-      float mx = fmax3f(__uint_as_float(sr[0]), __uint_as_float(sr[1]), __uint_as_float(sr[2]));
+      float mxa = fmax3f(__uint_as_float(sr[0]), __uint_as_float(sr[1]), __uint_as_float(sr[2]));
+      float mxb = fmax3f(__uint_as_float(sr[3]), __uint_as_float(sr[4]), __uint_as_float(sr[5]));
+      float mxc = fmax3f(__uint_as_float(sr[6]), __uint_as_float(sr[7]), __uint_as_float(sr[8]));
+      float mxd = fmax3f(__uint_as_float(sr[9]), __uint_as_float(sr[10]), __uint_as_float(sr[11]));
 #pragma unroll
-      for (int c = 3; c < BN - 1; c += 2)
-        mx = fmax3f(mx, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
-      mx = fmaxf(mx, __uint_as_float(sr[BN - 1]));
+      for (int c = 12; c < 60; c += 8) {
+        mxa = fmax3f(mxa, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        mxb = fmax3f(mxb, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+        mxc = fmax3f(mxc, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+        mxd = fmax3f(mxd, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+      }
+      mxa = fmax3f(mxa, __uint_as_float(sr[60]), __uint_as_float(sr[61]));
+      mxb = fmax3f(mxb, __uint_as_float(sr[62]), __uint_as_float(sr[63]));
+      const float mx = fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd));
       const float mx_s = mx * sl;
+      // Lazy rescale: the reference max moves only when the row max grows by
+      // more than 2^8; O and the running sum are then scaled by alpha.
       bool need = false;
-      float m_new = m_run;
+      float alpha = 1.0f;
       if (j == 0) {
         m_run = mx_s;
       } else if (mx_s > m_run + 8.0f) {
         need = true;
-        m_new = mx_s;
+        alpha = ex2_approx(m_run - mx_s);
+        m_run = mx_s;
       }
-      if (__any_sync(0xffffffffu, need)) {
-        // O_l must hold PV_l(j - 1) before it is rescaled.
-        if (!wait_all(b_pvdone(ln), (j - 1) & 1)) { ok = false; break; }
-        tc_fence_after();
-        const float alpha = need ? ex2_approx(m_run - m_new) : 1.0f;
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          TM_TMEM_LD32(tO + c * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          TM_TMEM_ST32(tO + c * 32, o);
-        }
-        tmem_wait_st();
-        l_run *= alpha;
-        m_run = m_new;
-      }
-      const uint64_t sl2 = f2_packf(sl, sl);
       const uint64_t nm2 = f2_packf(-m_run, -m_run);
       uint64_t acc[4] = {0, 0, 0, 0};
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int c = 0; c < BN; c += 2) {
-        float x0, x1;
+        float x0, x1, p0, p1;
         f2_unpack(f2_fma(f2_pack(sr[c], sr[c + 1]), sl2, nm2), x0, x1);
-        const float p0 = ex2_approx(x0);
-        const float p1 = ex2_approx(x1);
+        if (((c >> 1) & 3) < kEmulPairs) {
+          exp2_poly2(x0, x1, p0, p1);
+        } else {
+          p0 = ex2_approx(x0);
+          p1 = ex2_approx(x1);
+        }
         acc[(c >> 1) & 3] = f2_add(acc[(c >> 1) & 3], f2_packf(p0, p1));
         pk[c >> 1] = pack_bf16x2(p0, p1);
       }
       float a0, a1, a2, a3;
       f2_unpack(f2_add(acc[0], acc[1]), a0, a1);
       f2_unpack(f2_add(acc[2], acc[3]), a2, a3);
-      l_run += (a0 + a1) + (a2 + a3);
-      // P_l overwrites the first 64 columns of S_l (S is already in registers).
-      TM_TMEM_ST32(tS + 0, (pk + 0));
-      TM_TMEM_ST32(tS + 32, (pk + 32));
+      l_run = l_run * alpha + ((a0 + a1) + (a2 + a3));
+      if (__any_sync(0xffffffffu, need)) {
+        // O_l must hold PV(j - 1) before it is rescaled; PV(j) is issued only
+        // after this thread's p_full arrival below.
+        if (!wait_all(b_pvdone(ln, (j - 1) & 1), ((j - 1) >> 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t o[16];
+          TM_TMEM_LD16(tO + c * 16, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          TM_TMEM_ST16(tO + c * 16, o);
+        }
+      }
+      // P buffer (j & 1) is free once PV(j - 2) has completed.
+      if (j >= 2) {
+        if (!wait_all(b_pvdone(ln, j & 1), ((j - 2) >> 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+      }
+      TM_TMEM_ST32(tP + (j & 1) * 32, pk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(b_pfull(ln));
+      mbar_arrive(b_pfull(ln, j & 1));
     }
     // the final PV of this lane
-    const bool fin = ok && my_n > 0 && wait_all(b_pvdone(ln), (my_n - 1) & 1);
-    if (ln == 1) {
+    const bool fin =
+        ok && my_n > 0 && wait_all(b_pvdone(ln, (my_n - 1) & 1), ((my_n - 1) >> 1) & 1);
+    if (split && ln == 1) {
       m1_smem[row] = fin ? m_run : -INFINITY;
       l1_smem[row] = fin ? l_run : 0.f;
     }
     named_bar_sync(1, 256);
-    if (ln == 0 && fin) {
-      // lane 1 has finished all its PV (it waited before the barrier), or had none
-      const bool ok1 = (n1 == 0) || wait_all(b_pvdone(1), (n1 - 1) & 1);
-      if (ok1) {
-        tc_fence_after();
+    const bool writer = split ? (ln == 0) : true;
+    bool ok1 = true;
+    if (split && ln == 0 && fin)
+      ok1 = (n1 == 0) || wait_all(b_pvdone(1, (n1 - 1) & 1), ((n1 - 1) >> 1) & 1);
+    if (writer && fin && ok1) {
+      tc_fence_after();
+      float s0 = 1.0f / l_run, s1 = 0.f;
+      const bool merge = split && n1 > 0;
+      if (merge) {
         const float m1 = m1_smem[row], l1 = l1_smem[row];
         const float m = fmaxf(m_run, m1);
         const float c0 = ex2_approx(m_run - m);
-        const float c1 = (n1 > 0 && l1 > 0.f) ? ex2_approx(m1 - m) : 0.f;
+        const float c1 = l1 > 0.f ? ex2_approx(m1 - m) : 0.f;
         const float inv = 1.0f / (l_run * c0 + l1 * c1);
-        const float s0 = c0 * inv, s1 = c1 * inv;
-        const int qi = q_tile * BM + row;
-        __nv_bfloat16* orow = p.out + static_cast<int64_t>(batch) * p.out_bs +
-                              static_cast<int64_t>(qi) * p.out_rs +
-                              static_cast<int64_t>(head) * D;
-        const uint32_t tO1 = t_lane + C::kOCol + D;
+        s0 = c0 * inv;
+        s1 = c1 * inv;
+      }
+      __nv_bfloat16* orow = p.out + static_cast<int64_t>(batch) * p.out_bs +
+                            static_cast<int64_t>(qi) * p.out_rs + static_cast<int64_t>(head) * D;
+      const uint32_t tO1 = t_lane + C::kOCol + D;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32], o1[32];
-          TM_TMEM_LD32(tO + c * 32, o);
-          if (n1 > 0) {
-            TM_TMEM_LD32(tO1 + c * 32, o1);
-          } else {
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32], o1[32];
+        TM_TMEM_LD32(tO + c * 32, o);
+        if (merge) {
+          TM_TMEM_LD32(tO1 + c * 32, o1);
+        } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o1[i] = 0u;
-          }
-          tmem_wait_ld();
-          if (qi < p.Lq) {
+          for (int i = 0; i < 32; ++i) o1[i] = 0u;
+        }
+        tmem_wait_ld();
+        if (qi < p.Lq) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              float f[8];
+          for (int i = 0; i < 32; i += 8) {
+            float f[8];
 #pragma unroll
-              for (int k = 0; k < 8; ++k)
-                f[k] = __uint_as_float(o[i + k]) * s0 + __uint_as_float(o1[i + k]) * s1;
-              const uint4 v = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
-                                         pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
-              *reinterpret_cast<uint4*>(orow + c * 32 + i) = v;
-            }
+            for (int k = 0; k < 8; ++k)
+              f[k] = __uint_as_float(o[i + k]) * s0 + __uint_as_float(o1[i + k]) * s1;
+            const uint4 v = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                       pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+            *reinterpret_cast<uint4*>(orow + c * 32 + i) = v;
           }
         }
       }
@@ -404,9 +478,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 }
 
 // Encode a [B, rows, H, D] bf16 tensor (heads contiguous) as a 4-D TMA map
-// with a {64, 1, 128, 1} box and 128-byte swizzle.
+// with a {64, 1, box_rows, 1} box and 128-byte swizzle; rows past `rows` read
+// as zero.
 static int make_map(CUtensorMap* m, const void* base, int64_t rows, int B, int H, int D,
-                    int64_t batch_stride, int64_t row_stride, const char* what) {
+                    int64_t batch_stride, int64_t row_stride, int box_rows, const char* what) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return set_error(TM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   if (B == 1) batch_stride = rows * row_stride;
@@ -414,7 +489,7 @@ static int make_map(CUtensorMap* m, const void* base, int64_t rows, int B, int H
                         static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(B)};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(row_stride) * 2,
                            static_cast<cuuint64_t>(batch_stride) * 2};
-  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -438,7 +513,10 @@ static int launch(Params& prm, int B, int Lq, int H, cudaStream_t stream) {
     if (st) return st;
     configured[dev] = true;
   }
-  dim3 grid((Lq + BM - 1) / BM, H, B);
+  // pair CTAs (two query tiles of a head each), then the odd tile's split CTA,
+  // head-minor so that every head's pair CTAs launch before any split CTA
+  const int nq = (Lq + BM - 1) / BM;
+  dim3 grid(H, nq / 2 + (nq & 1), B);
   attn_fwd_kernel<D><<<grid, kThreads, C::kSmemAlloc, stream>>>(prm);
   return check_cuda(cudaGetLastError(), "attention: launch");
 }
@@ -458,7 +536,7 @@ extern "C" int tm_attention_fwd(const void* q, int64_t q_batch_stride, int64_t q
                                 int H, int D, float scale, void* stream) {
   using namespace tmb::attn;
   if (D != 64 && D != 128) return set_error(TM_ERR_UNSUPPORTED, "attention: head dim %d", D);
-  if (B < 1 || Lq < 1 || H < 1 || B > 65535 || H > 65535)
+  if (B < 1 || Lq < 1 || H < 1 || B > 65535 || H > 65535 || (Lq + 255) / 256 > 65535)
     return set_error(TM_ERR_INVALID_ARGUMENT, "attention: B=%d Lq=%d H=%d", B, Lq, H);
   if (!q || !out || !spans || n_spans < 1)
     return set_error(TM_ERR_INVALID_ARGUMENT, "attention: null pointer or no spans");
@@ -516,16 +594,18 @@ extern "C" int tm_attention_fwd(const void* q, int64_t q_batch_stride, int64_t q
     if (rs_of[s] < (int64_t)H * D)
       return set_error(TM_ERR_INVALID_ARGUMENT, "attention: source %d row stride < H*D", s);
   }
-  int st = make_map(&prm.tm_q, q, Lq, B, H, D, q_batch_stride, q_row_stride, "q");
-  if (st) return st;
+  int st = TM_OK;
   for (int s = 0; s < 2; ++s) {
     const int src = use_src[s] ? s : (use_src[0] ? 0 : 1);  // unused slot: copy a valid map
-    st = make_map(&prm.tm_k[s], kp[src], rows_of[src], B, H, D, bs_of[src], rs_of[src], "k");
+    st = make_map(&prm.tm_k[s], kp[src], rows_of[src], B, H, D, bs_of[src], rs_of[src], BN, "k");
     if (st) return st;
-    st = make_map(&prm.tm_v[s], vp[src], rows_of[src], B, H, D, bs_of[src], rs_of[src], "v");
+    st = make_map(&prm.tm_v[s], vp[src], rows_of[src], B, H, D, bs_of[src], rs_of[src], BN, "v");
     if (st) return st;
   }
+  st = make_map(&prm.tm_q, q, Lq, B, H, D, q_batch_stride, q_row_stride, BM, "q");
+  if (st) return st;
   prm.n_tiles = nt;
+  prm.n_qtiles = (Lq + BM - 1) / BM;
   prm.Lq = Lq;
   prm.out = static_cast<__nv_bfloat16*>(out);
   prm.out_bs = (B == 1) ? 0 : out_batch_stride;
