@@ -90,15 +90,14 @@ struct Cfg {
   static constexpr int kVOff = kKOff + kKStages * kKVBytes;
   static constexpr int kBarOff = kVOff + kVStages * kKVBytes;
   // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
-  //           s_full[2], s_free[2], p_full[2][2], pv_done[2][2], drain[2]
+  //           s_full[2][2], p_full[2][2], pv_done[2][2], drain[2]
   static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 14;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
   static constexpr int kMLOff = kMiscOff + 16;             // lane-1 max / sum per row
   static constexpr int kSmemBytes = kMLOff + 2 * BM * 4;
   static constexpr int kSmemAlloc = kSmemBytes + 1024;     // runtime 1 KB alignment slack
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kSCol = 0;     // S_l at kSCol + 64 l
-  static constexpr uint32_t kPCol = 128;   // P_l,b at kPCol + 64 l + 32 b
+  static constexpr uint32_t kSCol = 0;     // S_l,b at kSCol + 128 l + 64 b; P over its first 32
   static constexpr uint32_t kOCol = 256;   // O_l at kOCol + D l
 };
 
@@ -154,8 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   auto b_vfull = [&](int s) { return bar0 + 8u * (1 + 2 * KS + s); };
   auto b_vempty = [&](int s) { return bar0 + 8u * (1 + 2 * KS + VS + s); };
   const uint32_t bar1 = bar0 + 8u * (1 + 2 * KS + 2 * VS);
-  auto b_sfull = [&](int l) { return bar1 + 8u * l; };
-  auto b_sfree = [&](int l) { return bar1 + 8u * (2 + l); };
+  auto b_sfull = [&](int l, int b) { return bar1 + 8u * (2 * l + b); };
   auto b_pfull = [&](int l, int b) { return bar1 + 8u * (4 + 2 * l + b); };
   auto b_pvdone = [&](int l, int b) { return bar1 + 8u * (8 + 2 * l + b); };
   auto b_drain = [&](int l) { return bar1 + 8u * (12 + l); };
@@ -180,9 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       mbar_init(b_vempty(s), consumers);
     }
     for (int l = 0; l < 2; ++l) {
-      mbar_init(b_sfull(l), 1);
-      mbar_init(b_sfree(l), 128);
       for (int b = 0; b < 2; ++b) {
+        mbar_init(b_sfull(l, b), 1);
         mbar_init(b_pfull(l, b), 128);
         mbar_init(b_pvdone(l, b), 1);
       }
@@ -251,58 +248,75 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     }
   } else if (warp == 1 || warp == 3) {
     // ------------------------------------------------------------------ MMA issuers
+    // The whole warp runs the loop (waits, descriptor arithmetic) so that
+    // every value stays warp-uniform; one elected lane issues the MMAs and
+    // their commits.
     const int l = warp == 1 ? 0 : 1;
     const int nl = l == 0 ? n0 : n1;
-    if (lane_id == 0 && nl > 0) {
+    if (nl > 0) {
       constexpr uint32_t idesc_qk = idesc_bf16_f32(BM, BN, 0);
       constexpr uint32_t idesc_pv = idesc_bf16_f32(BM, D, 1);
+      const bool leader = elect_one();
       const int qsel = split ? 0 : l;
       // Descriptors are built once; per tile and K-step only the start
       // address field (bytes >> 4, low bits) moves.
       const uint64_t qd = smem_desc_sw128(sbase + C::kQOff + qsel * C::kQBytes, 16, 1024);
       const uint64_t kd0 = smem_desc_sw128(sbase + C::kKOff, 16, 1024);
       const uint64_t vd0 = smem_desc_sw128(sbase + C::kVOff, C::kBlk, 1024);
-      const uint32_t tS = tmem + C::kSCol + l * BN;
-      const uint32_t tP = tmem + C::kPCol + l * 64;
+      const uint32_t tS = tmem + C::kSCol + l * 128;  // + 64 b: S / P buffer b
       const uint32_t tO = tmem + C::kOCol + l * D;
-      bool ok = mbar_wait(b_qfull, 0, abort_flag, p.err);
-      for (int j = 0; ok && j <= nl; ++j) {
-        if (j < nl) {
-          const int g = item_of(l, j);
-          const int s = g % KS;
-          if (!mbar_wait(b_kfull(s), (g / KS) & 1, abort_flag, p.err)) { ok = false; break; }
-          if (j > 0 && !mbar_wait(b_sfree(l), (j - 1) & 1, abort_flag, p.err)) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t kd = kd0 + static_cast<uint64_t>(s * (C::kKVBytes >> 4));
+      auto wait_w = [&](uint32_t bar, uint32_t par) -> bool {
+        const bool w = mbar_wait_spin(bar, par, abort_flag, p.err);
+        return __all_sync(0xffffffffu, w);
+      };
+      // QK(j) into S buffer j & 1; the buffer is free once PV(j - 2), which
+      // read P(j - 2) from it, has completed.
+      auto qk = [&](int j) -> bool {
+        const int g = item_of(l, j);
+        const int s = g % KS;
+        if (!wait_w(b_kfull(s), (g / KS) & 1)) return false;
+        tc_fence_after();
+        const uint64_t kd = kd0 + static_cast<uint64_t>(s * (C::kKVBytes >> 4));
+        if (leader) {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t qo = ((kk >> 2) * C::kQBlk + (kk & 3) * 32) >> 4;
             const uint32_t ko = ((kk >> 2) * C::kBlk + (kk & 3) * 32) >> 4;
-            umma_ss(tS, qd + qo, kd + ko, idesc_qk, kk > 0 ? 1u : 0u);
+            umma_ss(tS + (j & 1) * 64, qd + qo, kd + ko, idesc_qk, kk > 0 ? 1u : 0u);
           }
-          umma_commit(b_sfull(l));
+          umma_commit(b_sfull(l, j & 1));
           umma_commit(b_kempty(s));
         }
-        if (j > 0) {
-          const int jp = j - 1;
-          const int g = item_of(l, jp);
-          const int s = g % VS;
-          const int b = jp & 1;
-          if (!mbar_wait(b_pfull(l, b), (jp >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
-          if (!mbar_wait(b_vfull(s), (g / VS) & 1, abort_flag, p.err)) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t vd = vd0 + static_cast<uint64_t>(s * (C::kKVBytes >> 4));
+        __syncwarp();
+        return true;
+      };
+      bool ok = wait_w(b_qfull, 0) && qk(0) && (nl < 2 || qk(1));
+      for (int jp = 0; ok && jp < nl; ++jp) {
+        const int g = item_of(l, jp);
+        const int s = g % VS;
+        const int b = jp & 1;
+        if (!wait_w(b_pfull(l, b), (jp >> 1) & 1)) { ok = false; break; }
+        if (!wait_w(b_vfull(s), (g / VS) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t vd = vd0 + static_cast<uint64_t>(s * (C::kKVBytes >> 4));
+        if (leader) {
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk)
-            umma_ts(tO, tP + b * 32 + kk * 8, vd + static_cast<uint64_t>(kk * (2048 >> 4)),
+            umma_ts(tO, tS + b * 64 + kk * 8, vd + static_cast<uint64_t>(kk * (2048 >> 4)),
                     idesc_pv, (jp > 0 || kk > 0) ? 1u : 0u);
           umma_commit(b_pvdone(l, b));
           umma_commit(b_vempty(s));
         }
+        __syncwarp();
+        if (jp + 2 < nl) {
+          if (!wait_w(b_pvdone(l, b), (jp >> 1) & 1)) { ok = false; break; }
+          if (!qk(jp + 2)) { ok = false; break; }
+        }
       }
       if (!ok) {
-        // Drain: wait for every MMA this thread issued before TMEM is released.
-        umma_commit(b_drain(l));
+        // Drain: wait for every MMA the leader issued before TMEM is released.
+        if (leader) umma_commit(b_drain(l));
+        __syncwarp();
         mbar_wait(b_drain(l), 0, nullptr, p.err, 100000000ull);
       }
     }
@@ -313,8 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane_id;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
-    const uint32_t tS = t_lane + C::kSCol + ln * BN;
-    const uint32_t tP = t_lane + C::kPCol + ln * 64;
+    const uint32_t tS = t_lane + C::kSCol + ln * 128;  // + 64 (j & 1)
     const uint32_t tO = t_lane + C::kOCol + ln * D;
     const int my_n = ln == 0 ? n0 : n1;
     const int tile0 = (split && ln == 1) ? n0 : 0;
@@ -328,14 +341,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     };
     const uint64_t sl2 = f2_packf(sl, sl);
     for (int j = 0; j < my_n; ++j) {
-      if (!wait_all(b_sfull(ln), j & 1)) { ok = false; break; }
+      if (!wait_all(b_sfull(ln, j & 1), (j >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
+      const uint32_t tSj = tS + (j & 1) * 64;
       uint32_t sr[BN];
-      TM_TMEM_LD32(tS + 0, (sr + 0));
-      TM_TMEM_LD32(tS + 32, (sr + 32));
+      TM_TMEM_LD32(tSj + 0, (sr + 0));
+      TM_TMEM_LD32(tSj + 32, (sr + 32));
       tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(b_sfree(ln));  // S_l may now be overwritten by QK(j + 1)
 
       const int valid = p.tiles[tile0 + j].y;
       if (valid < BN) {
@@ -404,12 +416,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           TM_TMEM_ST16(tO + c * 16, o);
         }
       }
-      // P buffer (j & 1) is free once PV(j - 2) has completed.
-      if (j >= 2) {
-        if (!wait_all(b_pvdone(ln, j & 1), ((j - 2) >> 1) & 1)) { ok = false; break; }
-        tc_fence_after();
-      }
-      TM_TMEM_ST32(tP + (j & 1) * 32, pk);
+      // P(j) over the first half of its own S buffer (S(j) is in registers;
+      // the next MMA to write this buffer waits for PV(j)).
+      TM_TMEM_ST32(tSj, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(b_pfull(ln, j & 1));

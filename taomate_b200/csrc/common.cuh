@@ -68,6 +68,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// One lane of a converged warp (elect.sync); the same lane on every call.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Non-blocking test: has the phase with the given parity completed?
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -92,6 +103,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0u) {
+      if (abort != nullptr && *abort) return false;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        if (abort != nullptr) *abort = 1;
+        atomicCAS(err, 0, kDevWaitTimeout);
+        return false;
+      }
+    }
+  }
+}
+
+// Same contract as mbar_wait, polling with the non-blocking test instead of
+// try_wait (no suspend / resume latency; costs issue slots while it spins).
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, volatile int* abort,
+                                               int* err,
+                                               unsigned long long limit_ns = kWaitLimitNs) {
+  if (mbar_test(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_test(bar, parity)) return true;
+    if ((i & 255u) == 0u) {
       if (abort != nullptr && *abort) return false;
       if (globaltimer_ns() - t0 > limit_ns) {
         if (abort != nullptr) *abort = 1;
