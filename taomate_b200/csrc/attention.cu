@@ -18,7 +18,7 @@
 // takes P from TMEM.
 //
 // Warp roles (12 warps):
-//   warp 0      TMA producer of Q and of the K ring (no multicast).
+//   warp 0      TMA producer of Q and of the K ring (plain tile loads).
 //   warp 2      TMA producer of the V ring.
 //   warp 1 / 3  tcgen05.mma issuers of lane 0 / lane 1, one thread each: a
 //               single thread issues at most one MMA every ~50 cycles, so a

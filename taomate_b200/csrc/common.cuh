@@ -134,7 +134,7 @@ __device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, vo
 }
 
 // ---------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), no multicast.
+// TMA (cp.async.bulk.tensor): plain tile loads into this CTA only.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

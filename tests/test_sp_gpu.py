@@ -1,0 +1,100 @@
+"""Ulysses sequence parallelism over NCCL on 2 GPUs (skipped with fewer).
+
+Each rank holds its shard of the chunk's tokens and a head shard of the KV
+cache over the whole sequence, as the reference lays them out
+(ltx_causal/transformer/kv_cache.py:331-339, 1432-1462, 1535-1538).
+``attention_with_cache`` with the packed seq->head exchange and the head->seq
+exchange must reproduce the single-GPU call on the same inputs: the output rows
+of the rank's token shard and the new K/V of the rank's heads.  The only
+difference allowed is the projection GEMMs' bf16 rounding on a different
+number of rows.
+"""
+
+import datetime
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+WORLD = 2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, outdir):
+    sys.path.insert(0, os.path.dirname(HERE))
+    import taomate_b200 as tm
+    from taomate_b200 import parallel as P
+    from taomate_b200.attention import AttentionWeights
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        heads, dim_head, frames, fh, fw = 8, 128, 2, 8, 12
+        hidden, lq, lc = heads * dim_head, frames * fh * fw, 320
+        torch.manual_seed(0)  # identical weights on both ranks
+        attn = AttentionWeights(hidden, heads, dim_head, gated=True, device=dev)
+        g = torch.Generator(device=dev).manual_seed(1)
+        x = torch.randn(1, lq, hidden, device=dev, generator=g).to(torch.bfloat16)
+        ck = torch.randn(1, lc, heads, dim_head, device=dev, generator=g).to(torch.bfloat16)
+        cv = torch.randn(1, lc, heads, dim_head, device=dev, generator=g).to(torch.bfloat16)
+        cos, sin = tm.causal_precompute_freqs_cis(torch.tensor([[frames, fh, fw]]), hidden,
+                                                  start_frame=3, device=dev,
+                                                  dtype=torch.bfloat16,
+                                                  num_attention_heads=heads)
+        with torch.no_grad():
+            ref_out, ref_k, ref_v = tm.attention_with_cache(attn, x, None, (cos, sin), None,
+                                                            ck, cv)
+        P.init_sp_mesh(world, world)
+        sl, hl = lq // world, heads // world
+        ts = slice(rank * sl, (rank + 1) * sl)
+        hs = slice(rank * hl, (rank + 1) * hl)
+        with torch.no_grad():
+            out, nk, nv = tm.attention_with_cache(
+                attn, x[:, ts].contiguous(), None, (cos[:, :, ts], sin[:, :, ts]), None,
+                ck[:, :, hs].contiguous(), cv[:, :, hs].contiguous())
+        torch.cuda.synchronize()
+        f = lambda t: t.float().cpu().numpy()
+        np.savez(os.path.join(outdir, f"r{rank}.npz"), out=f(out), ref_out=f(ref_out[:, ts]),
+                 k=f(nk), ref_k=f(ref_k[:, :, hs]), v=f(nv), ref_v=f(ref_v[:, :, hs]))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _rel_l2(a, b):
+    a = a.astype(np.float64)
+    b = b.astype(np.float64)
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_ulysses_sp2_matches_single_gpu(tmp_path):
+    mp.spawn(_worker, args=(WORLD, _free_port(), str(tmp_path)), nprocs=WORLD, join=True)
+    for r in range(WORLD):
+        z = np.load(tmp_path / f"r{r}.npz")
+        assert z["out"].shape == z["ref_out"].shape
+        assert z["k"].shape == z["ref_k"].shape
+        # bf16 rounding of the projections on half the rows; everything after
+        # them (norm, RoPE, exchange, attention) is the same arithmetic
+        assert _rel_l2(z["k"], z["ref_k"]) < 5e-3
+        assert _rel_l2(z["v"], z["ref_v"]) < 5e-3
+        assert _rel_l2(z["out"], z["ref_out"]) < 1e-2
