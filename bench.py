@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--kernel-case", choices=["attention", "norm_rope"], default=None,
                     help="time one kernel in isolation at C2 shapes (profiling target)")
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--heads", type=int, default=None,
+                    help="--kernel-case attention: heads per GPU (32 / sequence-parallel ranks)")
     return ap.parse_args()
 
 
@@ -395,12 +397,13 @@ def run_kernel_case(args):
     Lc = (ANCHOR_FRAMES + WINDOW_FRAMES) * FRAME_TOKENS
     rnd = lambda *s: torch.randn(*s, device=dev, generator=g).to(torch.bfloat16)
     if args.kernel_case == "attention":
-        q = rnd(1, Lq, HEADS, DIM_HEAD)
-        ck, cv = rnd(1, Lc, HEADS, DIM_HEAD), rnd(1, Lc, HEADS, DIM_HEAD)
-        nk, nv = rnd(1, Lq, HEADS, DIM_HEAD), rnd(1, Lq, HEADS, DIM_HEAD)
+        Hk = args.heads or HEADS
+        q = rnd(1, Lq, Hk, DIM_HEAD)
+        ck, cv = rnd(1, Lc, Hk, DIM_HEAD), rnd(1, Lc, Hk, DIM_HEAD)
+        nk, nv = rnd(1, Lq, Hk, DIM_HEAD), rnd(1, Lq, Hk, DIM_HEAD)
         out = torch.empty_like(q)
         fn = lambda: tm.flash_attention(q, ck, cv, [(0, Lc)], nk, nv, Lq, out=out)
-        work, unit = 4.0 * Lq * (Lc + Lq) * HEADS * DIM_HEAD / 1e12, "TFLOP/s"
+        work, unit = 4.0 * Lq * (Lc + Lq) * Hk * DIM_HEAD / 1e12, "TFLOP/s"
     else:
         xq, xk = rnd(1, Lq, HIDDEN), rnd(1, Lq, HIDDEN)
         w = torch.ones(HIDDEN, device=dev, dtype=torch.bfloat16)
@@ -427,7 +430,8 @@ def run_kernel_case(args):
     torch.cuda.synchronize()
     ms = sorted(a.elapsed_time(b) for a, b in ev)
     med = ms[len(ms) // 2]
-    print(json.dumps({"kernel_case": args.kernel_case, "median_ms": med, "min_ms": ms[0],
+    print(json.dumps({"kernel_case": args.kernel_case, "heads": args.heads or HEADS,
+                      "median_ms": med, "min_ms": ms[0],
                       "achieved": work / (med * 1e-3), "unit": unit}), flush=True)
 
 

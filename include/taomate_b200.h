@@ -168,6 +168,34 @@ TM_API int tm_attention_fwd(const void* q, int64_t q_batch_stride, int64_t q_row
                      int64_t out_batch_stride, int64_t out_row_stride, int B, int Lq, int H,
                      int D, float scale, void* stream);
 
+/*
+ * A7, same contract as tm_attention_fwd plus a caller-owned device workspace.
+ * When the query chunk has too few (head, query tile) pairs to occupy every
+ * SM (few heads per GPU under sequence parallelism, or a short chunk such as
+ * V2A's 25 audio queries against the video keys), the kernel divides each
+ * query tile's key tiles into ranges, one CTA each, writes normalised fp32
+ * partial outputs with their (max, sum) into the workspace and merges them
+ * in a second kernel.  workspace_bytes below what the best partition needs
+ * only limits the partition (0 / NULL never splits a key range).  The
+ * workspace is 16-byte aligned, not read before it is written, and must not
+ * be shared by calls that overlap on the GPU.  Same reference interface as
+ * tm_attention_fwd (flex_attention_utils.py:225-276).
+ */
+TM_API int tm_attention_fwd_ws(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
+                     const void* k_cache, const void* v_cache, int64_t cache_batch_stride,
+                     int64_t cache_row_stride, int64_t cache_rows, const void* k_new,
+                     const void* v_new, int64_t new_batch_stride, int64_t new_row_stride,
+                     int64_t new_rows, const tm_kv_span* spans, int n_spans, void* out,
+                     int64_t out_batch_stride, int64_t out_row_stride, int B, int Lq, int H,
+                     int D, float scale, void* workspace, int64_t workspace_bytes,
+                     void* stream);
+
+/*
+ * Workspace bytes tm_attention_fwd_ws uses for these shapes on the current
+ * device (0: no key-range split).  visible_keys = total rows of all spans.
+ */
+TM_API int64_t tm_attention_workspace_bytes(int B, int Lq, int H, int D, int64_t visible_keys);
+
 #ifdef __cplusplus
 }
 #endif

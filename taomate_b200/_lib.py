@@ -73,6 +73,13 @@ _SIGS = {
                                         ctypes.POINTER(KVSpan), ctypes.c_int, c_vp, c_i64, c_i64,
                                         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                         ctypes.c_float, c_vp]),
+    "tm_attention_fwd_ws": (ctypes.c_int, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
+                                           c_vp, c_vp, c_i64, c_i64, c_i64,
+                                           ctypes.POINTER(KVSpan), ctypes.c_int, c_vp, c_i64,
+                                           c_i64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                           ctypes.c_int, ctypes.c_float, c_vp, c_i64, c_vp]),
+    "tm_attention_workspace_bytes": (c_i64, [ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_int, c_i64]),
 }
 
 EXPORTED = tuple(_SIGS)

@@ -77,17 +77,38 @@ def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tens
             raise ValueError("new K and V must share strides")
         nrows = int(new_k.shape[1])
     lib = _lib.load()
+    keys = sum(n for (_, _, n) in spans)
+    ws_bytes = _workspace_bytes(lib, dev, B, Lq, H, D, keys)
+    # the key-range split's partial outputs live in a torch-owned workspace
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
     with torch.cuda.device(dev):
-        _lib.check(lib.tm_attention_fwd(
+        _lib.check(lib.tm_attention_fwd_ws(
             q.data_ptr(), qbs, qrs,
             cache_k.data_ptr() if cache_k is not None else None,
             cache_v.data_ptr() if cache_v is not None else None, cbs, crs, crows,
             new_k.data_ptr() if new_k is not None else None,
             new_v.data_ptr() if new_v is not None else None, nbs, nrs, nrows,
             arr, len(spans), out.data_ptr(), obs, ors, B, Lq, H, D,
-            float(scale) if scale is not None else 0.0, _lib.stream_ptr(dev)), "attention")
-        _lib.launched()
+            float(scale) if scale is not None else 0.0,
+            ws.data_ptr() if ws is not None else None, ws_bytes, _lib.stream_ptr(dev)),
+            "attention")
+        _lib.launched(2 if ws_bytes else 1)  # + the merge kernel of a key-range split
     return out
+
+
+_WS_CACHE = {}
+
+
+def _workspace_bytes(lib, dev, B, Lq, H, D, keys) -> int:
+    """Bytes of partial outputs the kernel's work partition needs for this
+    shape on this device (0 when it keeps every key range in one CTA)."""
+    key = (dev.index, B, Lq, H, D, keys)
+    n = _WS_CACHE.get(key)
+    if n is None:
+        with torch.cuda.device(dev):
+            n = int(lib.tm_attention_workspace_bytes(B, Lq, H, D, keys))
+        _WS_CACHE[key] = n
+    return n
 
 
 def standard_attention_forward(q: Tensor, k: Tensor, v: Tensor, mask: Optional[Tensor] = None,

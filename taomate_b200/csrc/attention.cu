@@ -10,6 +10,11 @@
 //              and lane 0 merges the two partial results.  Split CTAs come
 //              after the pair CTAs in grid order, so they fill the tail of the
 //              wave.
+// When pair CTAs would leave SMs idle (few heads per GPU under sequence
+// parallelism, or a short query chunk), every CTA is a split CTA for one
+// query tile, and with a workspace the key tiles are further divided into
+// kv_splits ranges, one CTA each; those CTAs write normalised fp32 partial
+// outputs with their (max, sum), and a combine kernel merges the ranges.
 //
 // Shared memory: the query tile(s) (TMA, 128-byte swizzle), a 4-stage K ring
 // and a 5-stage V ring of 64-key tiles.  TMEM (512 columns): S_l at 64 l
@@ -42,6 +47,8 @@
 // Reference semantics: softmax(Q K^T / sqrt(D)) V without a mask over
 // cat(cached, new) (ltx_causal/transformer/kv_cache.py:1486-1531,
 // ltx_causal/attention/flex_attention_utils.py:225-276).
+#include <algorithm>
+#include <climits>
 #include <cmath>
 #include <vector>
 
@@ -64,6 +71,10 @@ constexpr int kRegsSoftmax = 208;
 constexpr int kEmulPairs = 1;
 
 struct __align__(64) Params {
+  float* part_o;          // kv_splits > 1: [kv_splits][B][Lq][H][D] normalised partial outputs
+  float2* part_ml;        //                [kv_splits][B][Lq][H] (max * log2 scale, sum)
+  int mode;               // 0: pair CTAs (+ one split CTA for an odd tile); 1: split CTAs only
+  int kv_splits;          // mode 1: key-tile ranges per query tile
   CUtensorMap tm_q;
   CUtensorMap tm_k[2];  // [TM_KV_SOURCE_CACHE], [TM_KV_SOURCE_NEW]
   CUtensorMap tm_v[2];
@@ -140,11 +151,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   const int head = blockIdx.x, cta = blockIdx.y, batch = blockIdx.z;
   const int n = p.n_tiles;
   const int pairs = p.n_qtiles >> 1;
-  const bool split = cta >= pairs;  // the odd last query tile
-  const int qt0 = 2 * cta;
-  // key tiles per lane; split: lane 0 [0, n0), lane 1 [n0, n); pair: both [0, n)
-  const int n0 = split ? (n + 1) >> 1 : n;
-  const int n1 = split ? n - n0 : n;
+  const bool single = p.mode == 1;
+  const int kvs = single ? p.kv_splits : 1;
+  const int sidx = single ? cta % kvs : 0;  // key range of this CTA
+  const bool split = single || cta >= pairs;
+  const int qt0 = single ? cta / kvs : 2 * cta;
+  // this CTA's key tiles [kb, kb + nr)
+  const int kb = static_cast<int>(static_cast<int64_t>(sidx) * n / kvs);
+  const int nr = static_cast<int>(static_cast<int64_t>(sidx + 1) * n / kvs) - kb;
+  // key tiles per lane; split: lane 0 [kb, kb + n0), lane 1 the rest; pair: both all
+  const int n0 = split ? (nr + 1) >> 1 : nr;
+  const int n1 = split ? nr - n0 : nr;
 
   const uint32_t bar0 = sbase + C::kBarOff;
   const uint32_t b_qfull = bar0;
@@ -163,7 +180,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   float* l1_smem = m1_smem + BM;
 
   // stream item -> key tile; lane step -> stream item
-  auto tile_of = [&](int g) { return split ? ((g & 1) ? n0 + (g >> 1) : (g >> 1)) : g; };
+  auto tile_of = [&](int g) {
+    return kb + (split ? ((g & 1) ? n0 + (g >> 1) : (g >> 1)) : g);
+  };
   auto item_of = [&](int l, int j) { return split ? 2 * j + l : j; };
 
   if (threadIdx.x == 0) {
@@ -221,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
                         db * 64, head, (qt0 + t) * BM, batch);
       }
       int last = -1;
-      for (int g = 0; g < n; ++g) {
+      for (int g = 0; g < nr; ++g) {
         const int s = g % S;
         if (g >= S && !mbar_wait(is_k ? b_kempty(s) : b_vempty(s), ((g / S) - 1) & 1, abort_flag,
                                  p.err))
@@ -330,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     const uint32_t tS = t_lane + C::kSCol + ln * 128;  // + 64 (j & 1)
     const uint32_t tO = t_lane + C::kOCol + ln * D;
     const int my_n = ln == 0 ? n0 : n1;
-    const int tile0 = (split && ln == 1) ? n0 : 0;
+    const int tile0 = kb + ((split && ln == 1) ? n0 : 0);
     const int qi = (split ? qt0 : qt0 + ln) * BM + row;
     const float sl = p.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;
@@ -448,9 +467,45 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         s0 = c0 * inv;
         s1 = c1 * inv;
       }
+      const uint32_t tO1 = t_lane + C::kOCol + D;
+      if (kvs > 1) {
+        // normalised partial output of this key range, and its (max, sum)
+        if (qi < p.Lq) {
+          const int64_t idx =
+              ((static_cast<int64_t>(sidx) * gridDim.z + batch) * p.Lq + qi) * gridDim.x + head;
+          float m_tot = m_run, l_tot = l_run;
+          if (merge) {
+            const float m1 = m1_smem[row], l1 = l1_smem[row];
+            m_tot = fmaxf(m_run, m1);
+            l_tot = l_run * ex2_approx(m_run - m_tot) + (l1 > 0.f ? l1 * ex2_approx(m1 - m_tot) : 0.f);
+          }
+          p.part_ml[idx] = make_float2(m_tot, l_tot);
+          float* prow = p.part_o + idx * D;
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32], o1[32];
+            TM_TMEM_LD32(tO + c * 32, o);
+            if (merge) {
+              TM_TMEM_LD32(tO1 + c * 32, o1);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o1[i] = 0u;
+            }
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              float4 v;
+              v.x = __uint_as_float(o[i]) * s0 + __uint_as_float(o1[i]) * s1;
+              v.y = __uint_as_float(o[i + 1]) * s0 + __uint_as_float(o1[i + 1]) * s1;
+              v.z = __uint_as_float(o[i + 2]) * s0 + __uint_as_float(o1[i + 2]) * s1;
+              v.w = __uint_as_float(o[i + 3]) * s0 + __uint_as_float(o1[i + 3]) * s1;
+              *reinterpret_cast<float4*>(prow + c * 32 + i) = v;
+            }
+          }
+        }
+      } else {
       __nv_bfloat16* orow = p.out + static_cast<int64_t>(batch) * p.out_bs +
                             static_cast<int64_t>(qi) * p.out_rs + static_cast<int64_t>(head) * D;
-      const uint32_t tO1 = t_lane + C::kOCol + D;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32], o1[32];
@@ -475,6 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           }
         }
       }
+      }
     }
   }
 
@@ -483,6 +539,57 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// Merge of the kv_splits key ranges: one warp per (batch, query row, head);
+// out = sum_s w_s O_s / sum_s w_s with w_s = l_s 2^(m_s - max_s m_s), O_s the
+// range's normalised output.
+template <int D>
+__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ part_o,
+                                                      const float2* __restrict__ part_ml, int kvs,
+                                                      int B, int Lq, int H,
+                                                      __nv_bfloat16* __restrict__ out,
+                                                      int64_t out_bs, int64_t out_rs) {
+  constexpr int kPer = D / 32;  // columns per lane
+  const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = static_cast<int64_t>(B) * Lq * H;
+  if (w >= total) return;
+  const int h = static_cast<int>(w % H);
+  const int qi = static_cast<int>((w / H) % Lq);
+  const int b = static_cast<int>(w / (static_cast<int64_t>(H) * Lq));
+  float mmax = -INFINITY;
+  for (int s = 0; s < kvs; ++s) mmax = fmaxf(mmax, part_ml[s * total + w].x);
+  float acc[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
+  float den = 0.f;
+  for (int s = 0; s < kvs; ++s) {
+    const float2 ml = part_ml[s * total + w];
+    const float wgt = ml.y * exp2f(ml.x - mmax);
+    den += wgt;
+    const float* src = part_o + (s * total + w) * D + lane * kPer;
+    if constexpr (kPer == 4) {
+      const float4 v = *reinterpret_cast<const float4*>(src);
+      acc[0] += wgt * v.x;
+      acc[1] += wgt * v.y;
+      acc[2] += wgt * v.z;
+      acc[3] += wgt * v.w;
+    } else {
+      const float2 v = *reinterpret_cast<const float2*>(src);
+      acc[0] += wgt * v.x;
+      acc[1] += wgt * v.y;
+    }
+  }
+  const float inv = 1.0f / den;
+  __nv_bfloat16* dst = out + static_cast<int64_t>(b) * out_bs + static_cast<int64_t>(qi) * out_rs +
+                       static_cast<int64_t>(h) * D + lane * kPer;
+  if constexpr (kPer == 4) {
+    *reinterpret_cast<uint2*>(dst) =
+        make_uint2(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv));
+  } else {
+    *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(acc[0] * inv, acc[1] * inv);
   }
 }
 
@@ -522,12 +629,70 @@ static int launch(Params& prm, int B, int Lq, int H, cudaStream_t stream) {
     if (st) return st;
     configured[dev] = true;
   }
-  // pair CTAs (two query tiles of a head each), then the odd tile's split CTA,
-  // head-minor so that every head's pair CTAs launch before any split CTA
+  // mode 0: pair CTAs (two query tiles of a head each), then the odd tile's
+  // split CTA, head-minor so that every head's pair CTAs launch before any
+  // split CTA.  mode 1: one CTA per (query tile, key range).
   const int nq = (Lq + BM - 1) / BM;
-  dim3 grid(H, nq / 2 + (nq & 1), B);
+  dim3 grid(H, prm.mode == 0 ? nq / 2 + (nq & 1) : nq * prm.kv_splits, B);
   attn_fwd_kernel<D><<<grid, kThreads, C::kSmemAlloc, stream>>>(prm);
-  return check_cuda(cudaGetLastError(), "attention: launch");
+  int st = check_cuda(cudaGetLastError(), "attention: launch");
+  if (st || prm.kv_splits <= 1) return st;
+  const int64_t warps = static_cast<int64_t>(B) * Lq * H;
+  combine_kernel<D><<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(
+      prm.part_o, prm.part_ml, prm.kv_splits, B, Lq, H, prm.out, prm.out_bs, prm.out_rs);
+  return check_cuda(cudaGetLastError(), "attention: combine launch");
+}
+
+// Work partition.  Costs are in units of one query tile against all visible
+// keys on one SM; CTAs start in grid order on the first free SM.
+struct Plan {
+  int mode;
+  int kv_splits;
+};
+
+static int64_t split_ws_bytes(int kvs, int B, int Lq, int H, int D) {
+  if (kvs <= 1) return 0;
+  const int64_t rows = static_cast<int64_t>(kvs) * B * Lq * H;
+  return rows * D * 4 + rows * 8 + 256;
+}
+
+static int sm_count() {
+  static int counts[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev < 0 || dev >= 64) return 148;
+  if (counts[dev] == 0) {
+    int c = 0;
+    if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0)
+      c = 148;
+    counts[dev] = c;
+  }
+  return counts[dev];
+}
+
+static Plan make_plan(int B, int Lq, int H, int D, int n_tiles, int64_t ws_bytes) {
+  const int sms = sm_count();
+  const int64_t nq = (Lq + BM - 1) / BM;
+  const int64_t heads = static_cast<int64_t>(H) * B;
+  const int64_t big = heads * (nq / 2), small = heads * (nq & 1);
+  // pair mode: 2-unit CTAs, then 1-unit CTAs
+  const int64_t waves_big = (big + sms - 1) / sms;
+  const double cost_pair =
+      std::max(2.0 * waves_big, std::ceil(static_cast<double>(2 * big + small) / sms));
+  Plan best{0, 1};
+  double best_cost = cost_pair;
+  const int s_max = std::max(1, std::min(32, n_tiles / 2));
+  for (int s = 1; s <= s_max; ++s) {
+    if (s > 1 && split_ws_bytes(s, B, Lq, H, D) > ws_bytes) break;
+    const int64_t ctas = heads * nq * s;
+    // the merge pass of s > 1 costs a little: require a clear gain
+    const double cost = std::ceil(static_cast<double>(ctas) / sms) / s * (s > 1 ? 1.08 : 1.0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = Plan{1, s};
+    }
+  }
+  return best;
 }
 
 }  // namespace attn
@@ -535,14 +700,14 @@ static int launch(Params& prm, int B, int Lq, int H, cudaStream_t stream) {
 
 using namespace tmb;
 
-extern "C" int tm_attention_fwd(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
-                                const void* k_cache, const void* v_cache,
-                                int64_t cache_batch_stride, int64_t cache_row_stride,
-                                int64_t cache_rows, const void* k_new, const void* v_new,
-                                int64_t new_batch_stride, int64_t new_row_stride, int64_t new_rows,
-                                const tm_kv_span* spans, int n_spans, void* out,
-                                int64_t out_batch_stride, int64_t out_row_stride, int B, int Lq,
-                                int H, int D, float scale, void* stream) {
+static int attention_impl(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
+                          const void* k_cache, const void* v_cache, int64_t cache_batch_stride,
+                          int64_t cache_row_stride, int64_t cache_rows, const void* k_new,
+                          const void* v_new, int64_t new_batch_stride, int64_t new_row_stride,
+                          int64_t new_rows, const tm_kv_span* spans, int n_spans, void* out,
+                          int64_t out_batch_stride, int64_t out_row_stride, int B, int Lq, int H,
+                          int D, float scale, void* workspace, int64_t workspace_bytes,
+                          void* stream) {
   using namespace tmb::attn;
   if (D != 64 && D != 128) return set_error(TM_ERR_UNSUPPORTED, "attention: head dim %d", D);
   if (B < 1 || Lq < 1 || H < 1 || B > 65535 || H > 65535 || (Lq + 255) / 256 > 65535)
@@ -623,6 +788,58 @@ extern "C" int tm_attention_fwd(const void* q, int64_t q_batch_stride, int64_t q
   prm.scale_log2 = static_cast<float>(sc * 1.4426950408889634);
   prm.err = device_error_flag();
   if (!prm.err) return set_error(TM_ERR_CUDA, "attention: device error flag unavailable");
+  if (workspace_bytes < 0 || (workspace_bytes > 0 && !workspace))
+    return set_error(TM_ERR_INVALID_ARGUMENT, "attention: bad workspace");
+  if (workspace && !aligned16(workspace))
+    return set_error(TM_ERR_ALIGNMENT, "attention: workspace not 16-byte aligned");
+  const Plan plan = make_plan(B, Lq, H, D, nt, workspace ? workspace_bytes : 0);
+  prm.mode = plan.mode;
+  prm.kv_splits = plan.kv_splits;
+  if (plan.kv_splits > 1) {
+    const int64_t rows = static_cast<int64_t>(plan.kv_splits) * B * Lq * H;
+    prm.part_o = static_cast<float*>(workspace);
+    uintptr_t ml = reinterpret_cast<uintptr_t>(prm.part_o + rows * D);
+    ml = (ml + 255) & ~static_cast<uintptr_t>(255);
+    prm.part_ml = reinterpret_cast<float2*>(ml);
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return D == 128 ? launch<128>(prm, B, Lq, H, s) : launch<64>(prm, B, Lq, H, s);
+}
+
+extern "C" int tm_attention_fwd(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
+                                const void* k_cache, const void* v_cache,
+                                int64_t cache_batch_stride, int64_t cache_row_stride,
+                                int64_t cache_rows, const void* k_new, const void* v_new,
+                                int64_t new_batch_stride, int64_t new_row_stride, int64_t new_rows,
+                                const tm_kv_span* spans, int n_spans, void* out,
+                                int64_t out_batch_stride, int64_t out_row_stride, int B, int Lq,
+                                int H, int D, float scale, void* stream) {
+  return attention_impl(q, q_batch_stride, q_row_stride, k_cache, v_cache, cache_batch_stride,
+                        cache_row_stride, cache_rows, k_new, v_new, new_batch_stride,
+                        new_row_stride, new_rows, spans, n_spans, out, out_batch_stride,
+                        out_row_stride, B, Lq, H, D, scale, nullptr, 0, stream);
+}
+
+extern "C" int tm_attention_fwd_ws(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
+                                   const void* k_cache, const void* v_cache,
+                                   int64_t cache_batch_stride, int64_t cache_row_stride,
+                                   int64_t cache_rows, const void* k_new, const void* v_new,
+                                   int64_t new_batch_stride, int64_t new_row_stride,
+                                   int64_t new_rows, const tm_kv_span* spans, int n_spans,
+                                   void* out, int64_t out_batch_stride, int64_t out_row_stride,
+                                   int B, int Lq, int H, int D, float scale, void* workspace,
+                                   int64_t workspace_bytes, void* stream) {
+  return attention_impl(q, q_batch_stride, q_row_stride, k_cache, v_cache, cache_batch_stride,
+                        cache_row_stride, cache_rows, k_new, v_new, new_batch_stride,
+                        new_row_stride, new_rows, spans, n_spans, out, out_batch_stride,
+                        out_row_stride, B, Lq, H, D, scale, workspace, workspace_bytes, stream);
+}
+
+extern "C" int64_t tm_attention_workspace_bytes(int B, int Lq, int H, int D,
+                                                int64_t visible_keys) {
+  using namespace tmb::attn;
+  if (B < 1 || Lq < 1 || H < 1 || (D != 64 && D != 128) || visible_keys < 1) return 0;
+  const int64_t tiles = std::min<int64_t>((visible_keys + BN - 1) / BN, kMaxTiles);
+  const Plan plan = make_plan(B, Lq, H, D, static_cast<int>(tiles), INT64_MAX);
+  return split_ws_bytes(plan.kv_splits, B, Lq, H, D);
 }

@@ -197,6 +197,12 @@ ATTN_SHAPES = [
     (4, 64, 96, 576, [(0, 576)], 96),                    # C1 shapes
     (2, 128, 1, 7, [(0, 7)], 1),                         # single query, 8 keys
     (8, 128, 300, 1000, [(5, 3), (100, 129), (400, 255)], 17),  # odd spans
+    # C2 head shards under sequence parallelism: 16, 8 and 4 heads per GPU
+    # (split CTAs only; key ranges over 2 and 4 CTAs merged by the combine pass)
+    (16, 128, 1152, 3456, [(0, 3456)], 1152),
+    (8, 128, 1152, 3456, [(0, 3456)], 1152),
+    (4, 128, 1152, 6144, [(0, 384), (1536, 3072)], 1152),
+    (1, 64, 25, 0, [], 4608),                            # V2A with one head per GPU
 ]
 
 
@@ -413,3 +419,30 @@ def test_arena_attention_matches_tensor_cache():
     out = tm.flash_attention(q, ck, cv, spans, nk, nv, 1152)
     km, vm = k.materialize(), v.materialize()
     assert_attention_parity(out, q, [km, nk], [vm, nv])
+
+
+def test_attention_key_range_split_and_plain_entry_agree():
+    """The workspace entry point splits key ranges across CTAs when the grid
+    is small; the plain entry point keeps each range in one CTA.  Both meet
+    the parity bar and agree with each other to bf16 rounding."""
+    from taomate_b200 import _lib, flash_attention
+    lib = _lib.load()
+    H, D, Lq, Lk = 4, 128, 1152, 4608
+    assert lib.tm_attention_workspace_bytes(1, Lq, H, D, Lk) > 0
+    assert lib.tm_attention_workspace_bytes(1, Lq, 32, D, Lk) == 0
+    gen = torch.Generator().manual_seed(11)
+    q = torch.randn(1, Lq, H, D, generator=gen).to(DEV, torch.bfloat16)
+    k = torch.randn(1, Lk, H, D, generator=gen).to(DEV, torch.bfloat16)
+    v = torch.randn(1, Lk, H, D, generator=gen).to(DEV, torch.bfloat16)
+    out_ws = flash_attention(q, None, None, [], k, v, Lk)
+    out_plain = torch.empty_like(q)
+    spans = (_lib.KVSpan * 1)()
+    spans[0].source, spans[0].row_start, spans[0].rows = 1, 0, Lk
+    st = lib.tm_attention_fwd(q.data_ptr(), 0, H * D, None, None, 0, 0, 0, k.data_ptr(),
+                              v.data_ptr(), 0, H * D, Lk, spans, 1, out_plain.data_ptr(), 0,
+                              H * D, 1, Lq, H, D, 0.0, _lib.stream_ptr(q.device))
+    assert st == 0, lib.tm_last_error()
+    torch.cuda.synchronize()
+    assert_attention_parity(out_ws, q, [k], [v])
+    assert_attention_parity(out_plain, q, [k], [v])
+    assert rel_l2(out_ws, out_plain) < 4e-3
