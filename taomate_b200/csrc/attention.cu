@@ -469,29 +469,32 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       }
       const uint32_t tO1 = t_lane + C::kOCol + D;
       if (kvs > 1) {
-        // normalised partial output of this key range, and its (max, sum)
-        if (qi < p.Lq) {
-          const int64_t idx =
-              ((static_cast<int64_t>(sidx) * gridDim.z + batch) * p.Lq + qi) * gridDim.x + head;
-          float m_tot = m_run, l_tot = l_run;
-          if (merge) {
-            const float m1 = m1_smem[row], l1 = l1_smem[row];
-            m_tot = fmaxf(m_run, m1);
-            l_tot = l_run * ex2_approx(m_run - m_tot) + (l1 > 0.f ? l1 * ex2_approx(m1 - m_tot) : 0.f);
-          }
-          p.part_ml[idx] = make_float2(m_tot, l_tot);
-          float* prow = p.part_o + idx * D;
+        // Normalised partial output of this key range, and its (max, sum).
+        // The TMEM loads are warp-collective: every lane runs them, rows past
+        // Lq only skip the stores.
+        const bool live = qi < p.Lq;
+        const int64_t idx =
+            ((static_cast<int64_t>(sidx) * gridDim.z + batch) * p.Lq + qi) * gridDim.x + head;
+        float m_tot = m_run, l_tot = l_run;
+        if (merge) {
+          const float m1 = m1_smem[row], l1 = l1_smem[row];
+          m_tot = fmaxf(m_run, m1);
+          l_tot = l_run * ex2_approx(m_run - m_tot) + (l1 > 0.f ? l1 * ex2_approx(m1 - m_tot) : 0.f);
+        }
+        if (live) p.part_ml[idx] = make_float2(m_tot, l_tot);
+        float* prow = p.part_o + idx * D;
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32], o1[32];
-            TM_TMEM_LD32(tO + c * 32, o);
-            if (merge) {
-              TM_TMEM_LD32(tO1 + c * 32, o1);
-            } else {
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32], o1[32];
+          TM_TMEM_LD32(tO + c * 32, o);
+          if (merge) {
+            TM_TMEM_LD32(tO1 + c * 32, o1);
+          } else {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) o1[i] = 0u;
-            }
-            tmem_wait_ld();
+            for (int i = 0; i < 32; ++i) o1[i] = 0u;
+          }
+          tmem_wait_ld();
+          if (live) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
               float4 v;
