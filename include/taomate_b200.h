@@ -196,6 +196,33 @@ TM_API int tm_attention_fwd_ws(const void* q, int64_t q_batch_stride, int64_t q_
  */
 TM_API int64_t tm_attention_workspace_bytes(int B, int Lq, int H, int D, int64_t visible_keys);
 
+/*
+ * No counterpart in the reference: an addition of this library.
+ *
+ * tm_attention_fwd_ws for callers that cannot allocate device memory: a
+ * host program that embeds this library in a runtime owning every byte of
+ * the GPU (memory reserved up front, no allocator offered to plugins), or a
+ * latency-critical path where cudaMalloc's implicit synchronisation is not
+ * allowed.  The caller still passes q, K/V and out; the key-range split's
+ * scratch is a fixed 16 MiB array in the library's own device memory, which
+ * every GPU that loads the library keeps until the process exits.  Shapes
+ * whose split needs more (tm_attention_workspace_bytes > 16 MiB) are
+ * rejected with TM_ERR_INVALID_ARGUMENT.
+ *   - The first call on a device looks up the array's device address (with
+ *     that device current); make that first call before any stream capture.
+ *   - All calls share the one array: calls that overlap on the GPU (other
+ *     streams, other threads) race on it.  Serialise them.
+ *   - Nothing has to be cleared between calls: each call writes every
+ *     scratch row it reads.
+ */
+TM_API int tm_attention_fwd_noalloc(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
+                     const void* k_cache, const void* v_cache, int64_t cache_batch_stride,
+                     int64_t cache_row_stride, int64_t cache_rows, const void* k_new,
+                     const void* v_new, int64_t new_batch_stride, int64_t new_row_stride,
+                     int64_t new_rows, const tm_kv_span* spans, int n_spans, void* out,
+                     int64_t out_batch_stride, int64_t out_row_stride, int B, int Lq, int H,
+                     int D, float scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -50,6 +50,7 @@
 #include <algorithm>
 #include <climits>
 #include <cmath>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -845,4 +846,76 @@ extern "C" int64_t tm_attention_workspace_bytes(int B, int Lq, int H, int D,
   const int64_t tiles = std::min<int64_t>((visible_keys + BN - 1) / BN, kMaxTiles);
   const Plan plan = make_plan(B, Lq, H, D, static_cast<int>(tiles), INT64_MAX);
   return split_ws_bytes(plan.kv_splits, B, Lq, H, D);
+}
+
+// ---------------------------------------------------------------------------
+// Entry point for callers that cannot allocate device memory.  Its scratch
+// (the key-range split's partial outputs) lives in a fixed array in this
+// library's own device memory, so each GPU that loads the library holds
+// kNoAllocScratchBytes of it until the process exits.  Host code must not pass
+// the array's name to a kernel: on the host it only stands in for the symbol.
+// The device address is looked up with cudaGetSymbolAddress once per device,
+// with that device current, on the first call made on it.
+namespace tmb {
+namespace attn {
+
+constexpr int64_t kNoAllocScratchBytes = int64_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* ptrs[64] = {nullptr};
+  int dev = 0;
+  int st = check_cuda(cudaGetDevice(&dev), "attention (no-alloc): current device");
+  if (st) return st;
+  if (dev < 0 || dev >= 64)
+    return set_error(TM_ERR_UNSUPPORTED, "attention (no-alloc): device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    st = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch),
+                    "attention (no-alloc): address of the fixed scratch");
+    if (st) return st;
+    ptrs[dev] = p;
+  }
+  *out = ptrs[dev];
+  return TM_OK;
+}
+
+}  // namespace attn
+}  // namespace tmb
+
+extern "C" int tm_attention_fwd_noalloc(const void* q, int64_t q_batch_stride,
+                                        int64_t q_row_stride, const void* k_cache,
+                                        const void* v_cache, int64_t cache_batch_stride,
+                                        int64_t cache_row_stride, int64_t cache_rows,
+                                        const void* k_new, const void* v_new,
+                                        int64_t new_batch_stride, int64_t new_row_stride,
+                                        int64_t new_rows, const tm_kv_span* spans, int n_spans,
+                                        void* out, int64_t out_batch_stride,
+                                        int64_t out_row_stride, int B, int Lq, int H, int D,
+                                        float scale, void* stream) {
+  using namespace tmb::attn;
+  if (!spans || n_spans < 1)
+    return set_error(TM_ERR_INVALID_ARGUMENT, "attention: null pointer or no spans");
+  int64_t keys = 0;
+  for (int i = 0; i < n_spans; ++i)
+    if (spans[i].rows > 0) keys += spans[i].rows;
+  const int64_t need = tm_attention_workspace_bytes(B, Lq, H, D, keys);
+  if (need > kNoAllocScratchBytes)
+    return set_error(TM_ERR_INVALID_ARGUMENT,
+                     "attention (no-alloc): B=%d Lq=%d H=%d D=%d over %lld keys needs %lld bytes "
+                     "of scratch, above the fixed %lld bytes; use tm_attention_fwd_ws",
+                     B, Lq, H, D, (long long)keys, (long long)need,
+                     (long long)kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  const int st = noalloc_scratch(&scratch);
+  if (st) return st;
+  // Every row the merge pass reads is written first in the same call, so
+  // nothing left in the array by an earlier call needs clearing.
+  return attention_impl(q, q_batch_stride, q_row_stride, k_cache, v_cache, cache_batch_stride,
+                        cache_row_stride, cache_rows, k_new, v_new, new_batch_stride,
+                        new_row_stride, new_rows, spans, n_spans, out, out_batch_stride,
+                        out_row_stride, B, Lq, H, D, scale, scratch, kNoAllocScratchBytes,
+                        stream);
 }
