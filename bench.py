@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="issue every forward from Python instead of replaying a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-case", choices=["attention", "norm_rope"], default=None,
                     help="time one kernel in isolation at C2 shapes (profiling target)")
@@ -222,6 +224,7 @@ def run_ours(args):
     from taomate_b200 import _lib, parallel as P
     from taomate_b200.attention import AttentionWeights
     from taomate_b200.cache import retain_window
+    from taomate_b200.graphs import AttentionGraph, attention_spans
     from taomate_b200.kv_cache import ArenaSpec, KVCache, LayerKVCache, init_arena_cache
     from taomate_b200.profiler import TIMER
 
@@ -279,7 +282,57 @@ def run_ours(args):
                 cache = retain_window(KVCache(layers=new_layers), anchor, window)
         return cache
 
-    def timed(n_steps, n_warm, host_io):
+    def tables(block):
+        cos, sin = tm.causal_precompute_freqs_cis(grid, HIDDEN, start_frame=block * Q_FRAMES,
+                                                  device=dev, dtype=torch.bfloat16,
+                                                  num_attention_heads=HEADS)
+        return (cos[:, :, rank * S_loc:(rank + 1) * S_loc],
+                sin[:, :, rank * S_loc:(rank + 1) * S_loc])
+
+    class GraphRunner:
+        """One captured 48-layer forward (all four forwards of a block are the
+        same computation over the same cache: the commit forward only keeps its
+        new K/V).  Captured at the steady state, where every call sees the same
+        number of key tiles; per block only the tile table, the RoPE tables and
+        the inputs change."""
+
+        def __init__(self, cache, block):
+            c, s = tables(block)
+            self.pe = (c.contiguous(), s.contiguous())
+            for lay in cache.layers:  # pending chunks go to their slots before capture
+                attention_spans(lay.video_self_k, lay.video_self_v, Lq)
+            self.graph = AttentionGraph(dev, max_sites=L)
+
+            def forward():
+                kv, out = [], None
+                for li in range(L):
+                    lay = cache.layers[li]
+                    out, nk, nv = tm.attention_with_cache(attn[li], xs[li], None, self.pe, None,
+                                                          lay.video_self_k, lay.video_self_v)
+                    kv.append((nk, nv))
+                return out, kv
+
+            self.out, self.kv = self.graph.capture(forward)
+
+        def step(self, cache, block, outs=None):
+            c, s = tables(block)  # once per block: the four forwards share the start frame
+            self.pe[0].copy_(c)
+            self.pe[1].copy_(s)
+            spans = [attention_spans(lay.video_self_k, lay.video_self_v, Lq)
+                     for lay in cache.layers]
+            for fwd in range(FORWARDS_PER_STEP):
+                self.graph.replay(spans if fwd == 0 else None)
+                if outs is not None:
+                    outs[fwd].copy_(self.out, non_blocking=True)
+            new_layers = []
+            for li, lay in enumerate(cache.layers):
+                nk, nv = self.kv[li]
+                k2, v2 = tm.cat_cache_pair(lay.video_self_k, lay.video_self_v, nk, nv)
+                k2.entries()  # into its slot now: the next replay rewrites nk / nv
+                new_layers.append(LayerKVCache(video_self_k=k2, video_self_v=v2))
+            return retain_window(KVCache(layers=new_layers), anchor, window)
+
+    def timed(n_steps, n_warm, host_io, graphed=False):
         cache = fresh_cache()
         x_host = outs = None
         if host_io:
@@ -288,10 +341,13 @@ def run_ours(args):
             outs = [torch.empty(1, S_loc, HIDDEN, dtype=torch.bfloat16).pin_memory()
                     for _ in range(FORWARDS_PER_STEP)]
         block = 0
+        runner = None
         with torch.no_grad():
             for _ in range(n_warm):
                 cache = step(cache, block)
                 block += 1
+            if graphed:
+                runner = GraphRunner(cache, block)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -305,7 +361,12 @@ def run_ours(args):
         e0.record()
         with torch.no_grad():
             for _ in range(n_steps):
-                if host_io:
+                if runner is not None:
+                    if host_io:  # the captured forward reads xs
+                        for li in range(L):
+                            xs[li].copy_(x_host[li], non_blocking=True)
+                    cache = runner.step(cache, block, outs)
+                elif host_io:
                     for li in range(L):
                         x_dev[li].copy_(x_host[li], non_blocking=True)
                     cache = step(cache, block, x_dev, outs)
@@ -325,15 +386,23 @@ def run_ours(args):
             dist.barrier()
         h2d = sum(x.numel() * x.element_size() for x in xs) if host_io else 0
         d2h = FORWARDS_PER_STEP * S_loc * HIDDEN * 2 if host_io else 0
+        if runner is not None:
+            runner.graph.reset()  # before the process group its exchanges use goes away
+            del runner
         return ms, launches, clocks, h2d, d2h
 
-    ms, launches, clocks, _, _ = timed(args.steps, args.warmup, host_io=False)
-    sections = TIMER.summary()
+    graphed = not args.eager
+    ms, launches, clocks, _, _ = timed(args.steps, args.warmup, host_io=False, graphed=graphed)
     value = Q_FRAMES * args.steps / (ms / 1e3)
+    if graphed:
+        # A replayed graph cannot bracket single kernels with events: the
+        # attention launches are timed in an eager pass of the same steps.
+        timed(args.steps, args.warmup, host_io=False, graphed=False)
+    sections = TIMER.summary()
 
     e2e = None
     if not args.no_e2e:
-        ems, _, _, h2d, d2h = timed(args.steps, args.warmup, host_io=True)
+        ems, _, _, h2d, d2h = timed(args.steps, args.warmup, host_io=True, graphed=graphed)
         e2e = {"value": Q_FRAMES * args.steps / (ems / 1e3), "unit": "latent frames/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": ems / args.steps}
@@ -373,6 +442,8 @@ def run_ours(args):
                        "layers": L, "q_tokens": Lq, "cached_tokens": anchor + window,
                        "keys_per_query": Lkv, "heads": HEADS, "dim_head": DIM_HEAD,
                        "parallelism": f"ulysses sp{sp}" if sp > 1 else "single gpu",
+                       "executor": "cuda graph per forward (eager warm-up, capture at the full "
+                                   "window)" if graphed else "eager",
                        "l2": "inputs larger than L2 (48 layers of weights, caches and "
                              "activations, ~14 GB), no flush"},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,

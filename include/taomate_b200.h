@@ -197,6 +197,35 @@ TM_API int tm_attention_fwd_ws(const void* q, int64_t q_batch_stride, int64_t q_
 TM_API int64_t tm_attention_workspace_bytes(int B, int Lq, int H, int D, int64_t visible_keys);
 
 /*
+ * The key-tile list the attention kernel walks for a span list: n_tiles pairs
+ * (source << 30 | first row, valid rows), 64 keys per tile, in span order.
+ * Validates the spans as tm_attention_fwd does.  Used to refresh the device
+ * tile table of tm_attention_fwd_dev_tiles between CUDA-graph replays.
+ */
+TM_API int tm_attention_tiles(const tm_kv_span* spans, int n_spans, int64_t cache_rows,
+                     int64_t new_rows, int32_t* tiles_out, int max_tiles, int* n_tiles);
+
+/*
+ * tm_attention_fwd_ws whose kernel reads its key-tile list from device memory
+ * (device_tiles, 16-byte aligned, in the tm_attention_tiles layout) instead of
+ * from its launch parameters.  `spans` fixes the tile count and the work
+ * partition at launch; the table may be rewritten before each replay of a
+ * captured graph as long as it keeps that tile count and each tile's source
+ * (both sources' pointers, when given, stay mapped).  Same reference
+ * interface as tm_attention_fwd (flex_attention_utils.py:225-276): it replaces
+ * the per-block cache concat of attention_with_cache (kv_cache.py:1486-1492)
+ * in a replayed forward.
+ */
+TM_API int tm_attention_fwd_dev_tiles(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
+                     const void* k_cache, const void* v_cache, int64_t cache_batch_stride,
+                     int64_t cache_row_stride, int64_t cache_rows, const void* k_new,
+                     const void* v_new, int64_t new_batch_stride, int64_t new_row_stride,
+                     int64_t new_rows, const tm_kv_span* spans, int n_spans,
+                     const void* device_tiles, void* out, int64_t out_batch_stride,
+                     int64_t out_row_stride, int B, int Lq, int H, int D, float scale,
+                     void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * No counterpart in the reference: an addition of this library.
  *
  * tm_attention_fwd_ws for callers that cannot allocate device memory: a

@@ -80,6 +80,14 @@ _SIGS = {
                                            ctypes.c_int, ctypes.c_float, c_vp, c_i64, c_vp]),
     "tm_attention_workspace_bytes": (c_i64, [ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                              ctypes.c_int, c_i64]),
+    "tm_attention_tiles": (ctypes.c_int, [ctypes.POINTER(KVSpan), ctypes.c_int, c_i64, c_i64,
+                                          c_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    "tm_attention_fwd_dev_tiles": (ctypes.c_int, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64,
+                                                  c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
+                                                  ctypes.POINTER(KVSpan), ctypes.c_int, c_vp, c_vp,
+                                                  c_i64, c_i64, ctypes.c_int, ctypes.c_int,
+                                                  ctypes.c_int, ctypes.c_int, ctypes.c_float, c_vp,
+                                                  c_i64, c_vp]),
     "tm_attention_fwd_noalloc": (ctypes.c_int, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64,
                                                 c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
                                                 ctypes.POINTER(KVSpan), ctypes.c_int, c_vp,

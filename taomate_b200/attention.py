@@ -24,6 +24,7 @@ import torch.nn.functional as F
 from torch import Tensor
 
 from . import _lib
+from . import graphs as _graphs
 from . import parallel as P
 from .kv_cache import ArenaKV, cache_rows_view
 from .profiler import section
@@ -81,6 +82,23 @@ def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tens
     ws_bytes = _workspace_bytes(lib, dev, B, Lq, H, D, keys)
     # the key-range split's partial outputs live in a torch-owned workspace
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+    rec = _graphs.recorder()
+    if rec is not None:
+        # captured into a graph: the key-tile list goes to the graph's device table
+        tiles = rec._add_site(arr, len(spans), crows, nrows)
+        with torch.cuda.device(dev):
+            _lib.check(lib.tm_attention_fwd_dev_tiles(
+                q.data_ptr(), qbs, qrs,
+                cache_k.data_ptr() if cache_k is not None else None,
+                cache_v.data_ptr() if cache_v is not None else None, cbs, crs, crows,
+                new_k.data_ptr() if new_k is not None else None,
+                new_v.data_ptr() if new_v is not None else None, nbs, nrs, nrows,
+                arr, len(spans), tiles, out.data_ptr(), obs, ors, B, Lq, H, D,
+                float(scale) if scale is not None else 0.0,
+                ws.data_ptr() if ws is not None else None, ws_bytes, _lib.stream_ptr(dev)),
+                "attention")
+            _lib.launched(2 if ws_bytes else 1)
+        return out
     with torch.cuda.device(dev):
         _lib.check(lib.tm_attention_fwd_ws(
             q.data_ptr(), qbs, qrs,

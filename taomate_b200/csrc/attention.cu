@@ -74,6 +74,7 @@ constexpr int kEmulPairs = 1;
 struct __align__(64) Params {
   float* part_o;          // kv_splits > 1: [kv_splits][B][Lq][H][D] normalised partial outputs
   float2* part_ml;        //                [kv_splits][B][Lq][H] (max * log2 scale, sum)
+  const int2* tiles_dev;  // non-null: read the key-tile list from device memory (graph replay)
   int mode;               // 0: pair CTAs (+ one split CTA for an odd tile); 1: split CTAs only
   int kv_splits;          // mode 1: key-tile ranges per query tile
   CUtensorMap tm_q;
@@ -181,6 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   float* l1_smem = m1_smem + BM;
 
   // stream item -> key tile; lane step -> stream item
+  const int2* tl = p.tiles_dev ? p.tiles_dev : p.tiles;
   auto tile_of = [&](int g) {
     return kb + (split ? ((g & 1) ? n0 + (g >> 1) : (g >> 1)) : g);
   };
@@ -246,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         if (g >= S && !mbar_wait(is_k ? b_kempty(s) : b_vempty(s), ((g / S) - 1) & 1, abort_flag,
                                  p.err))
           break;
-        const int2 tile = p.tiles[tile_of(g)];
+        const int2 tile = tl[tile_of(g)];
         const int src = tile.x >> 30;
         const int row = tile.x & 0x3FFFFFFF;
         const uint32_t full = is_k ? b_kfull(s) : b_vfull(s);
@@ -369,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       TM_TMEM_LD32(tSj + 32, (sr + 32));
       tmem_wait_ld();
 
-      const int valid = p.tiles[tile0 + j].y;
+      const int valid = tl[tile0 + j].y;
       if (valid < BN) {
 #pragma unroll
         for (int c = 0; c < BN; ++c)
@@ -704,6 +706,38 @@ static Plan make_plan(int B, int Lq, int H, int D, int n_tiles, int64_t ws_bytes
 
 using namespace tmb;
 
+// Key-tile list of a span list: (source << 30 | first row, valid rows), BN keys per tile.
+static int build_tiles(const tm_kv_span* spans, int n_spans, int64_t cache_rows, int64_t new_rows,
+                       int2* tiles, int* n_tiles, bool use_src[2]) {
+  using namespace tmb::attn;
+  int nt = 0;
+  int64_t total = 0;
+  for (int i = 0; i < n_spans; ++i) {
+    const tm_kv_span& s = spans[i];
+    if (s.source != TM_KV_SOURCE_CACHE && s.source != TM_KV_SOURCE_NEW)
+      return set_error(TM_ERR_INVALID_ARGUMENT, "attention: span %d has source %d", i, s.source);
+    const int64_t lim = s.source == TM_KV_SOURCE_CACHE ? cache_rows : new_rows;
+    if (s.rows < 0 || s.row_start < 0 || (int64_t)s.row_start + s.rows > lim)
+      return set_error(TM_ERR_INVALID_ARGUMENT,
+                       "attention: span %d [%d, +%d) outside source of %lld rows", i, s.row_start,
+                       s.rows, (long long)lim);
+    if (s.rows == 0) continue;
+    use_src[s.source] = true;
+    for (int off = 0; off < s.rows; off += BN) {
+      if (nt >= kMaxTiles)
+        return set_error(TM_ERR_INVALID_ARGUMENT, "attention: more than %d visible keys",
+                         kMaxTiles * BN);
+      tiles[nt].x = (s.source << 30) | (s.row_start + off);
+      tiles[nt].y = (s.rows - off) < BN ? (s.rows - off) : BN;
+      ++nt;
+    }
+    total += s.rows;
+  }
+  if (total == 0) return set_error(TM_ERR_INVALID_ARGUMENT, "attention: no visible keys");
+  *n_tiles = nt;
+  return TM_OK;
+}
+
 static int attention_impl(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
                           const void* k_cache, const void* v_cache, int64_t cache_batch_stride,
                           int64_t cache_row_stride, int64_t cache_rows, const void* k_new,
@@ -711,7 +745,7 @@ static int attention_impl(const void* q, int64_t q_batch_stride, int64_t q_row_s
                           int64_t new_rows, const tm_kv_span* spans, int n_spans, void* out,
                           int64_t out_batch_stride, int64_t out_row_stride, int B, int Lq, int H,
                           int D, float scale, void* workspace, int64_t workspace_bytes,
-                          void* stream) {
+                          void* stream, const void* device_tiles = nullptr) {
   using namespace tmb::attn;
   if (D != 64 && D != 128) return set_error(TM_ERR_UNSUPPORTED, "attention: head dim %d", D);
   if (B < 1 || Lq < 1 || H < 1 || B > 65535 || H > 65535 || (Lq + 255) / 256 > 65535)
@@ -735,29 +769,16 @@ static int attention_impl(const void* q, int64_t q_batch_stride, int64_t q_row_s
   memset(&prm, 0, sizeof(prm));
   bool use_src[2] = {false, false};
   int nt = 0;
-  int64_t total = 0;
-  for (int i = 0; i < n_spans; ++i) {
-    const tm_kv_span& s = spans[i];
-    if (s.source != TM_KV_SOURCE_CACHE && s.source != TM_KV_SOURCE_NEW)
-      return set_error(TM_ERR_INVALID_ARGUMENT, "attention: span %d has source %d", i, s.source);
-    const int64_t lim = s.source == TM_KV_SOURCE_CACHE ? cache_rows : new_rows;
-    if (s.rows < 0 || s.row_start < 0 || (int64_t)s.row_start + s.rows > lim)
-      return set_error(TM_ERR_INVALID_ARGUMENT,
-                       "attention: span %d [%d, +%d) outside source of %lld rows", i, s.row_start,
-                       s.rows, (long long)lim);
-    if (s.rows == 0) continue;
-    use_src[s.source] = true;
-    for (int off = 0; off < s.rows; off += BN) {
-      if (nt >= kMaxTiles)
-        return set_error(TM_ERR_INVALID_ARGUMENT, "attention: more than %d visible keys",
-                         kMaxTiles * BN);
-      prm.tiles[nt].x = (s.source << 30) | (s.row_start + off);
-      prm.tiles[nt].y = (s.rows - off) < BN ? (s.rows - off) : BN;
-      ++nt;
-    }
-    total += s.rows;
+  int st0 = build_tiles(spans, n_spans, cache_rows, new_rows, prm.tiles, &nt, use_src);
+  if (st0) return st0;
+  if (device_tiles) {
+    // the device table is rewritten between graph replays: map every given source
+    if (!aligned16(device_tiles))
+      return set_error(TM_ERR_ALIGNMENT, "attention: device tile table not 16-byte aligned");
+    use_src[0] = use_src[0] || (k_cache && v_cache);
+    use_src[1] = use_src[1] || (k_new && v_new);
+    prm.tiles_dev = static_cast<const int2*>(device_tiles);
   }
-  if (total == 0) return set_error(TM_ERR_INVALID_ARGUMENT, "attention: no visible keys");
   const void* kp[2] = {k_cache, k_new};
   const void* vp[2] = {v_cache, v_new};
   const int64_t rows_of[2] = {cache_rows, new_rows};
@@ -846,6 +867,41 @@ extern "C" int64_t tm_attention_workspace_bytes(int B, int Lq, int H, int D,
   const int64_t tiles = std::min<int64_t>((visible_keys + BN - 1) / BN, kMaxTiles);
   const Plan plan = make_plan(B, Lq, H, D, static_cast<int>(tiles), INT64_MAX);
   return split_ws_bytes(plan.kv_splits, B, Lq, H, D);
+}
+
+extern "C" int tm_attention_tiles(const tm_kv_span* spans, int n_spans, int64_t cache_rows,
+                                  int64_t new_rows, int32_t* tiles_out, int max_tiles,
+                                  int* n_tiles) {
+  using namespace tmb::attn;
+  if (!spans || n_spans < 1 || !tiles_out || !n_tiles)
+    return set_error(TM_ERR_INVALID_ARGUMENT, "attention tiles: null pointer or no spans");
+  int2 tmp[kMaxTiles];
+  bool use_src[2] = {false, false};
+  int nt = 0;
+  const int st = build_tiles(spans, n_spans, cache_rows, new_rows, tmp, &nt, use_src);
+  if (st) return st;
+  if (nt > max_tiles)
+    return set_error(TM_ERR_INVALID_ARGUMENT, "attention tiles: %d tiles, room for %d", nt,
+                     max_tiles);
+  memcpy(tiles_out, tmp, sizeof(int2) * nt);
+  *n_tiles = nt;
+  return TM_OK;
+}
+
+extern "C" int tm_attention_fwd_dev_tiles(
+    const void* q, int64_t q_batch_stride, int64_t q_row_stride, const void* k_cache,
+    const void* v_cache, int64_t cache_batch_stride, int64_t cache_row_stride, int64_t cache_rows,
+    const void* k_new, const void* v_new, int64_t new_batch_stride, int64_t new_row_stride,
+    int64_t new_rows, const tm_kv_span* spans, int n_spans, const void* device_tiles, void* out,
+    int64_t out_batch_stride, int64_t out_row_stride, int B, int Lq, int H, int D, float scale,
+    void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!device_tiles)
+    return set_error(TM_ERR_INVALID_ARGUMENT, "attention: null device tile table");
+  return attention_impl(q, q_batch_stride, q_row_stride, k_cache, v_cache, cache_batch_stride,
+                        cache_row_stride, cache_rows, k_new, v_new, new_batch_stride,
+                        new_row_stride, new_rows, spans, n_spans, out, out_batch_stride,
+                        out_row_stride, B, Lq, H, D, scale, workspace, workspace_bytes, stream,
+                        device_tiles);
 }
 
 // ---------------------------------------------------------------------------
