@@ -416,6 +416,9 @@ def run_ours(args):
         achieved = flops / (sd["mean_ms"] * 1e-3) / 1e12
         peak = float(peaks["bf16_tflops_sustained"])
         traffic = profiled_traffic()
+        if traffic is not None and H_loc != HEADS:
+            # the capture is the 32-head launch; per-head bytes (Q, K/V, out) scale with heads
+            traffic = traffic * H_loc / HEADS
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "traffic": traffic,
                 "kernel": "tm attention (tcgen05)", "launch_ms": sd["mean_ms"],
