@@ -57,6 +57,9 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--nccl-exchange", action="store_true",
+                    help="N>1: the Ulysses exchanges through NCCL all_to_all_single instead of "
+                         "the kernels' NVLink peer stores")
     ap.add_argument("--eager", action="store_true",
                     help="issue every forward from Python instead of replaying a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -243,6 +246,8 @@ def run_ours(args):
     if Lq % sp or HEADS % sp:
         raise SystemExit(f"{sp} ranks do not divide {Lq} tokens / {HEADS} heads")
     S_loc, H_loc = Lq // sp, HEADS // sp
+    if world > 1 and not args.nccl_exchange:
+        P.init_peer_exchange(1, S_loc, HEADS, DIM_HEAD)
     anchor, window = ANCHOR_FRAMES * FRAME_TOKENS, WINDOW_FRAMES * FRAME_TOKENS
 
     torch.manual_seed(0)  # identical weights on every rank
@@ -444,7 +449,10 @@ def run_ours(args):
                                    "forwards per 3-frame block",
                        "layers": L, "q_tokens": Lq, "cached_tokens": anchor + window,
                        "keys_per_query": Lkv, "heads": HEADS, "dim_head": DIM_HEAD,
-                       "parallelism": f"ulysses sp{sp}" if sp > 1 else "single gpu",
+                       "parallelism": (f"ulysses sp{sp}, exchanges "
+                                       + ("nccl all_to_all" if args.nccl_exchange
+                                          else "fused NVLink peer stores"))
+                                      if sp > 1 else "single gpu",
                        "executor": "cuda graph per forward (eager warm-up, capture at the full "
                                    "window)" if graphed else "eager",
                        "l2": "inputs larger than L2 (48 layers of weights, caches and "
@@ -456,6 +464,7 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        P.close_peer_exchange()
         dist.destroy_process_group()
 
 

@@ -104,6 +104,42 @@ TM_API int tm_norm_rope(const tm_norm_rope_job* jobs, int n_jobs, int B, int H, 
                  int sp_size, void* stream);
 
 /*
+ * A2+A3+A4. tm_norm_rope whose head group g (the heads rank g owns after the
+ * seq->head exchange) is stored group_delta[g] bytes away from the job's
+ * output address: with every rank's receive buffer mapped into this process
+ * (tm_peer_open) the exchange happens in the kernel's own stores over NVLink
+ * (_seq_to_head, all_to_all.py:125-151).  Offsets 16-byte aligned, sp_size <= 8.
+ */
+TM_API int tm_norm_rope_peer(const tm_norm_rope_job* jobs, int n_jobs, int B, int H, int D,
+                 float eps, int sp_size, const int64_t* group_delta, void* stream);
+
+/*
+ * A4/A8. NVLink peer memory for the fused Ulysses exchanges (no counterpart
+ * function in the reference, which calls torch.distributed.all_to_all_single,
+ * all_to_all.py:125-173).
+ *   tm_peer_alloc   device buffer (cleared) and its 64-byte CUDA IPC handle;
+ *   tm_peer_open    map another rank's buffer (same box) into this process;
+ *   tm_peer_close / tm_peer_free  undo them;
+ *   tm_peer_flag_bytes  size of a rank's flag buffer (flags, then this rank's
+ *                   epoch counters at byte tm_peer_flag_bytes() - 64);
+ *   tm_peer_signal  after this rank's stores: publish its next epoch of
+ *                   `slot` (0..3) in every rank's flag buffer (peer_flags[i] =
+ *                   rank i's flag buffer as mapped here);
+ *   tm_peer_wait    stream-ordered wait until every rank published that epoch;
+ *                   gives up after 2 s and records device error 2
+ *                   (tm_device_error) instead of hanging.
+ * At most 8 ranks.  Plain peer stores and loads; no multicast.
+ */
+TM_API int tm_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle);
+TM_API int tm_peer_free(void* ptr);
+TM_API int tm_peer_open(const void* ipc_handle, void** peer_ptr);
+TM_API int tm_peer_close(void* peer_ptr);
+TM_API int64_t tm_peer_flag_bytes(void);
+TM_API int tm_peer_signal(void* const* peer_flags, int n_ranks, int rank, void* counters, int slot,
+                   void* stream);
+TM_API int tm_peer_wait(const void* flags, int n_ranks, void* counters, int slot, void* stream);
+
+/*
  * A6/A11/A12. Row-span copies for the KV slot arena: commit-time append of a
  * chunk's K/V into a slot, compaction on eviction and materialisation of a
  * slot list into a contiguous [B, L, H, D] tensor.
@@ -195,6 +231,39 @@ TM_API int tm_attention_fwd_ws(const void* q, int64_t q_batch_stride, int64_t q_
  * device (0: no key-range split).  visible_keys = total rows of all spans.
  */
 TM_API int64_t tm_attention_workspace_bytes(int B, int Lq, int H, int D, int64_t visible_keys);
+
+/*
+ * Options of tm_attention_fwd_ext (zero-initialise, then set what is used):
+ *   device_tiles     key-tile table in device memory (tm_attention_tiles
+ *                    layout), as tm_attention_fwd_dev_tiles; NULL: from spans
+ *   workspace, _bytes  key-range split scratch, as tm_attention_fwd_ws
+ *   rows_per_rank    0: `out` holds all Lq rows.  > 0: the fused head->seq
+ *                    exchange of Ulysses parallelism: query row r is stored in
+ *                    rank r / rows_per_rank's output buffer at local row
+ *                    r % rows_per_rank (at most 8 ranks)
+ *   head_base        head index of this call's head 0 within an output row
+ *                    (out_row_stride >= (head_base + H) * D)
+ *   out_delta[i]     bytes from `out` to rank i's output buffer, mapped into
+ *                    this process (tm_peer_open); 0 for this rank
+ * Replaces the attention + head->seq all-to-all of attention_with_cache
+ * (kv_cache.py:1531-1538, all_to_all.py:154-173).
+ */
+typedef struct {
+  const void* device_tiles;
+  void* workspace;
+  int64_t workspace_bytes;
+  int32_t rows_per_rank;
+  int32_t head_base;
+  int64_t out_delta[8];
+} tm_attention_ext;
+
+TM_API int tm_attention_fwd_ext(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
+                     const void* k_cache, const void* v_cache, int64_t cache_batch_stride,
+                     int64_t cache_row_stride, int64_t cache_rows, const void* k_new,
+                     const void* v_new, int64_t new_batch_stride, int64_t new_row_stride,
+                     int64_t new_rows, const tm_kv_span* spans, int n_spans, void* out,
+                     int64_t out_batch_stride, int64_t out_row_stride, int B, int Lq, int H,
+                     int D, float scale, const tm_attention_ext* ext, void* stream);
 
 /*
  * The key-tile list the attention kernel walks for a span list: n_tiles pairs

@@ -43,6 +43,12 @@ class NormRopeJob(ctypes.Structure):
                 ("L", c_i64)]
 
 
+class AttentionExt(ctypes.Structure):
+    _fields_ = [("device_tiles", c_vp), ("workspace", c_vp), ("workspace_bytes", c_i64),
+                ("rows_per_rank", ctypes.c_int32), ("head_base", ctypes.c_int32),
+                ("out_delta", c_i64 * 8)]
+
+
 class CopySpan(ctypes.Structure):
     _fields_ = [("src", c_vp), ("dst", c_vp), ("rows", c_i64), ("src_row_stride", c_i64),
                 ("dst_row_stride", c_i64)]
@@ -88,6 +94,23 @@ _SIGS = {
                                                   c_i64, c_i64, ctypes.c_int, ctypes.c_int,
                                                   ctypes.c_int, ctypes.c_int, ctypes.c_float, c_vp,
                                                   c_i64, c_vp]),
+    "tm_norm_rope_peer": (ctypes.c_int, [ctypes.POINTER(NormRopeJob), ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int,
+                                         ctypes.POINTER(c_i64), c_vp]),
+    "tm_attention_fwd_ext": (ctypes.c_int, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
+                                            c_vp, c_vp, c_i64, c_i64, c_i64,
+                                            ctypes.POINTER(KVSpan), ctypes.c_int, c_vp, c_i64,
+                                            c_i64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, ctypes.c_float,
+                                            ctypes.POINTER(AttentionExt), c_vp]),
+    "tm_peer_alloc": (ctypes.c_int, [c_i64, ctypes.POINTER(c_vp), c_vp]),
+    "tm_peer_free": (ctypes.c_int, [c_vp]),
+    "tm_peer_open": (ctypes.c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "tm_peer_close": (ctypes.c_int, [c_vp]),
+    "tm_peer_flag_bytes": (c_i64, []),
+    "tm_peer_signal": (ctypes.c_int, [ctypes.POINTER(c_vp), ctypes.c_int, ctypes.c_int, c_vp,
+                                      ctypes.c_int, c_vp]),
+    "tm_peer_wait": (ctypes.c_int, [c_vp, ctypes.c_int, c_vp, ctypes.c_int, c_vp]),
     "tm_attention_fwd_noalloc": (ctypes.c_int, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64,
                                                 c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
                                                 ctypes.POINTER(KVSpan), ctypes.c_int, c_vp,

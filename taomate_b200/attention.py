@@ -17,6 +17,7 @@ Per call (video self-attention, C2 shapes):
 
 from __future__ import annotations
 
+import ctypes
 from typing import Optional, Sequence, Tuple
 
 import torch
@@ -43,18 +44,33 @@ def _row_strides(t: Tensor, H: int, D: int) -> Tuple[int, int]:
 def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tensor],
                     cache_spans: Sequence[Tuple[int, int]], new_k: Optional[Tensor],
                     new_v: Optional[Tensor], new_rows: int, scale: Optional[float] = None,
-                    out: Optional[Tensor] = None) -> Tensor:
+                    out: Optional[Tensor] = None, peer=None) -> Tensor:
     """``softmax(q K^T * scale) V`` with the keys of ``cache_spans`` (row ranges
     of ``cache_k/v``) followed by the first ``new_rows`` rows of ``new_k/v``.
-    All tensors ``[B, L, H, D]`` bf16 with contiguous heads."""
+    All tensors ``[B, L, H, D]`` bf16 with contiguous heads.
+
+    With ``peer`` (a :class:`taomate_b200.parallel.PeerExchange`) the kernel
+    stores each output row in its owner rank's ``peer.out`` (the fused
+    head->seq exchange); the caller then runs ``peer.exchange(1)`` and reads
+    ``peer.out``, which is also what this returns."""
     dev = _lib.require_cuda(q, cache_k, new_k)
     B, Lq, H, D = (int(v) for v in q.shape)
     if q.dtype != torch.bfloat16:
         raise TypeError(f"expected bfloat16, got {q.dtype}")
     qbs, qrs = _row_strides(q, H, D)
-    if out is None:
-        out = torch.empty(B, Lq, H, D, device=dev, dtype=torch.bfloat16)
-    obs, ors = _row_strides(out, H, D)
+    ext = _lib.AttentionExt()
+    if peer is not None:
+        if Lq != peer.sp * peer.S_loc or H != peer.Hl or D != peer.D or B != peer.B:
+            raise ValueError("attention output does not match the peer exchange's shapes")
+        out = peer.out
+        obs, ors = (out.stride(0) if B > 1 else 0), out.stride(1)
+        ext.rows_per_rank, ext.head_base = peer.S_loc, peer.rank * peer.Hl
+        for i in range(8):
+            ext.out_delta[i] = peer.delta["out"][i]
+    else:
+        if out is None:
+            out = torch.empty(B, Lq, H, D, device=dev, dtype=torch.bfloat16)
+        obs, ors = _row_strides(out, H, D)
     spans = [(0, int(s), int(n)) for (s, n) in cache_spans if n > 0]
     if new_k is not None and new_rows > 0:
         spans.append((1, 0, int(new_rows)))
@@ -81,35 +97,23 @@ def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tens
     keys = sum(n for (_, _, n) in spans)
     ws_bytes = _workspace_bytes(lib, dev, B, Lq, H, D, keys)
     # the key-range split's partial outputs live in a torch-owned workspace
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+    if ws_bytes:
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        ext.workspace, ext.workspace_bytes = ws.data_ptr(), ws_bytes
     rec = _graphs.recorder()
     if rec is not None:
         # captured into a graph: the key-tile list goes to the graph's device table
-        tiles = rec._add_site(arr, len(spans), crows, nrows)
-        with torch.cuda.device(dev):
-            _lib.check(lib.tm_attention_fwd_dev_tiles(
-                q.data_ptr(), qbs, qrs,
-                cache_k.data_ptr() if cache_k is not None else None,
-                cache_v.data_ptr() if cache_v is not None else None, cbs, crs, crows,
-                new_k.data_ptr() if new_k is not None else None,
-                new_v.data_ptr() if new_v is not None else None, nbs, nrs, nrows,
-                arr, len(spans), tiles, out.data_ptr(), obs, ors, B, Lq, H, D,
-                float(scale) if scale is not None else 0.0,
-                ws.data_ptr() if ws is not None else None, ws_bytes, _lib.stream_ptr(dev)),
-                "attention")
-            _lib.launched(2 if ws_bytes else 1)
-        return out
+        ext.device_tiles = rec._add_site(arr, len(spans), crows, nrows)
     with torch.cuda.device(dev):
-        _lib.check(lib.tm_attention_fwd_ws(
+        _lib.check(lib.tm_attention_fwd_ext(
             q.data_ptr(), qbs, qrs,
             cache_k.data_ptr() if cache_k is not None else None,
             cache_v.data_ptr() if cache_v is not None else None, cbs, crs, crows,
             new_k.data_ptr() if new_k is not None else None,
             new_v.data_ptr() if new_v is not None else None, nbs, nrs, nrows,
             arr, len(spans), out.data_ptr(), obs, ors, B, Lq, H, D,
-            float(scale) if scale is not None else 0.0,
-            ws.data_ptr() if ws is not None else None, ws_bytes, _lib.stream_ptr(dev)),
-            "attention")
+            float(scale) if scale is not None else 0.0, ctypes.byref(ext),
+            _lib.stream_ptr(dev)), "attention")
         _lib.launched(2 if ws_bytes else 1)  # + the merge kernel of a key-range split
     return out
 
@@ -211,7 +215,20 @@ def attention_with_cache(
             q = q * (s.unsqueeze(-1) if s.dim() == 3 else s.view(B, -1, 1, 1))
     else:
         same = (q.shape == k.shape == v.shape)
-        if same:
+        peer = P.get_peer_exchange()
+        if peer is not None and not (same and B == 1 and peer.fits(B, L, H, D)):
+            peer = None
+        if peer is not None:
+            # fused exchanges: the kernels store into the owner rank's buffers over NVLink
+            with section(base + ".rope_reshape"):
+                norm_rope([q, k, v], [attn.q_norm.weight, attn.k_norm.weight, None],
+                          [q_pe, kk_pe, None], H, D, eps_q, sp_size=sp_size, packed=True,
+                          peer=peer)
+            with section(base + ".a2a_seq2head"):
+                peer.exchange(0)
+            flat = peer.recv.view(sp_size * L, 3, H // sp_size, D)
+            q, k, v = (flat[:, i].unsqueeze(0) for i in range(3))
+        elif same:
             with section(base + ".rope_reshape"):
                 send = norm_rope([q, k, v], [attn.q_norm.weight, attn.k_norm.weight, None],
                                  [q_pe, kk_pe, None], H, D, eps_q, sp_size=sp_size, packed=True)
@@ -240,11 +257,23 @@ def attention_with_cache(
     ck, cv, spans = _cache_source(cached_k, cached_v)
     if q.stride(3) != 1 or q.stride(2) != D:
         q = q.contiguous()
+    peer = P.get_peer_exchange() if sp_size > 1 else None
+    if peer is not None and not (q.data_ptr() >= peer.recv.data_ptr() and
+                                 q.data_ptr() < peer.recv.data_ptr() + peer.recv.nbytes):
+        peer = None  # this call's exchange went through NCCL
     with section(base + ".sdpa"):
-        out = flash_attention(q, ck, cv, spans, k, v, nk_rows)
+        out = flash_attention(q, ck, cv, spans, k, v, nk_rows, peer=peer)
 
     # 5. head -> seq
-    if sp_size > 1:
+    if peer is not None:
+        # The returned cache K/V must outlive the receive buffer: copy them
+        # before signalling, since after it the peers may store the next
+        # call's rows there.
+        k, v = k.contiguous(), v.contiguous()
+        with section(base + ".a2a_head2seq"):
+            peer.exchange(1)
+        out = peer.out
+    elif sp_size > 1:
         with section(base + ".a2a_head2seq"):
             out = P.head_all_to_all_seq(out, P.get_sp_group(), sp_size)
 

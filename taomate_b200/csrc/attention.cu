@@ -86,6 +86,12 @@ struct __align__(64) Params {
   int Lq;
   int64_t out_bs, out_rs;  // elements
   __nv_bfloat16* out;
+  // Output row placement: query row r goes to rank r / rows_per_rank, local
+  // row r % rows_per_rank, head head_base + h, at `out` + out_delta[rank]
+  // bytes (peer buffers mapped into this process; 0 for this rank).
+  int rows_per_rank;
+  int head_base;
+  int64_t out_delta[8];
   float scale_log2;
   int* err;
 };
@@ -137,6 +143,21 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float&
   f2_unpack(pp, p0, p1);
   y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
   y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
+// Address of output row qi, head `head`, column 0.
+__device__ __forceinline__ __nv_bfloat16* out_row(__nv_bfloat16* out, int64_t out_bs,
+                                                  int64_t out_rs, int rows_per_rank,
+                                                  int head_base, const int64_t* delta, int batch,
+                                                  int qi, int head, int D) {
+  int rr = qi / rows_per_rank;
+  rr = rr < 0 ? 0 : (rr > 7 ? 7 : rr);
+  const int li = qi - rr * rows_per_rank;
+  return reinterpret_cast<__nv_bfloat16*>(
+      reinterpret_cast<char*>(out + static_cast<int64_t>(batch) * out_bs +
+                              static_cast<int64_t>(li) * out_rs +
+                              static_cast<int64_t>(head_base + head) * D) +
+      delta[rr]);
 }
 
 template <int D>
@@ -510,8 +531,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           }
         }
       } else {
-      __nv_bfloat16* orow = p.out + static_cast<int64_t>(batch) * p.out_bs +
-                            static_cast<int64_t>(qi) * p.out_rs + static_cast<int64_t>(head) * D;
+      __nv_bfloat16* orow = out_row(p.out, p.out_bs, p.out_rs, p.rows_per_rank, p.head_base,
+                                    p.out_delta, batch, qi, head, D);
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32], o1[32];
@@ -551,12 +572,18 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 // Merge of the kv_splits key ranges: one warp per (batch, query row, head);
 // out = sum_s w_s O_s / sum_s w_s with w_s = l_s 2^(m_s - max_s m_s), O_s the
 // range's normalised output.
+struct OutPlace {
+  __nv_bfloat16* out;
+  int64_t out_bs, out_rs;
+  int rows_per_rank, head_base;
+  int64_t delta[8];
+};
+
 template <int D>
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ part_o,
                                                       const float2* __restrict__ part_ml, int kvs,
                                                       int B, int Lq, int H,
-                                                      __nv_bfloat16* __restrict__ out,
-                                                      int64_t out_bs, int64_t out_rs) {
+                                                      const __grid_constant__ OutPlace op) {
   constexpr int kPer = D / 32;  // columns per lane
   const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -589,8 +616,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
     }
   }
   const float inv = 1.0f / den;
-  __nv_bfloat16* dst = out + static_cast<int64_t>(b) * out_bs + static_cast<int64_t>(qi) * out_rs +
-                       static_cast<int64_t>(h) * D + lane * kPer;
+  __nv_bfloat16* dst = out_row(op.out, op.out_bs, op.out_rs, op.rows_per_rank, op.head_base,
+                               op.delta, b, qi, h, D) + lane * kPer;
   if constexpr (kPer == 4) {
     *reinterpret_cast<uint2*>(dst) =
         make_uint2(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv));
@@ -644,8 +671,15 @@ static int launch(Params& prm, int B, int Lq, int H, cudaStream_t stream) {
   int st = check_cuda(cudaGetLastError(), "attention: launch");
   if (st || prm.kv_splits <= 1) return st;
   const int64_t warps = static_cast<int64_t>(B) * Lq * H;
+  OutPlace op;
+  op.out = prm.out;
+  op.out_bs = prm.out_bs;
+  op.out_rs = prm.out_rs;
+  op.rows_per_rank = prm.rows_per_rank;
+  op.head_base = prm.head_base;
+  for (int i = 0; i < 8; ++i) op.delta[i] = prm.out_delta[i];
   combine_kernel<D><<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(
-      prm.part_o, prm.part_ml, prm.kv_splits, B, Lq, H, prm.out, prm.out_bs, prm.out_rs);
+      prm.part_o, prm.part_ml, prm.kv_splits, B, Lq, H, op);
   return check_cuda(cudaGetLastError(), "attention: combine launch");
 }
 
@@ -738,15 +772,25 @@ static int build_tiles(const tm_kv_span* spans, int n_spans, int64_t cache_rows,
   return TM_OK;
 }
 
+static tm_attention_ext ext_ws(void* ws, int64_t bytes, const void* tiles = nullptr) {
+  tm_attention_ext e{};
+  e.workspace = ws;
+  e.workspace_bytes = bytes;
+  e.device_tiles = tiles;
+  return e;
+}
+
 static int attention_impl(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
                           const void* k_cache, const void* v_cache, int64_t cache_batch_stride,
                           int64_t cache_row_stride, int64_t cache_rows, const void* k_new,
                           const void* v_new, int64_t new_batch_stride, int64_t new_row_stride,
                           int64_t new_rows, const tm_kv_span* spans, int n_spans, void* out,
                           int64_t out_batch_stride, int64_t out_row_stride, int B, int Lq, int H,
-                          int D, float scale, void* workspace, int64_t workspace_bytes,
-                          void* stream, const void* device_tiles = nullptr) {
+                          int D, float scale, const tm_attention_ext& ext, void* stream) {
   using namespace tmb::attn;
+  void* workspace = ext.workspace;
+  const int64_t workspace_bytes = ext.workspace_bytes;
+  const void* device_tiles = ext.device_tiles;
   if (D != 64 && D != 128) return set_error(TM_ERR_UNSUPPORTED, "attention: head dim %d", D);
   if (B < 1 || Lq < 1 || H < 1 || B > 65535 || H > 65535 || (Lq + 255) / 256 > 65535)
     return set_error(TM_ERR_INVALID_ARGUMENT, "attention: B=%d Lq=%d H=%d", B, Lq, H);
@@ -809,6 +853,19 @@ static int attention_impl(const void* q, int64_t q_batch_stride, int64_t q_row_s
   prm.out = static_cast<__nv_bfloat16*>(out);
   prm.out_bs = (B == 1) ? 0 : out_batch_stride;
   prm.out_rs = out_row_stride;
+  prm.rows_per_rank = ext.rows_per_rank > 0 ? ext.rows_per_rank : Lq;
+  prm.head_base = ext.head_base;
+  if (ext.rows_per_rank < 0 || ext.head_base < 0 ||
+      (ext.rows_per_rank > 0 && (Lq + ext.rows_per_rank - 1) / ext.rows_per_rank > 8))
+    return set_error(TM_ERR_INVALID_ARGUMENT, "attention: output placement rows %d head %d",
+                     ext.rows_per_rank, ext.head_base);
+  if (out_row_stride < static_cast<int64_t>(ext.head_base + H) * D)
+    return set_error(TM_ERR_INVALID_ARGUMENT, "attention: output row stride below head_base+H");
+  for (int i = 0; i < 8; ++i) {
+    if (ext.out_delta[i] & 15)
+      return set_error(TM_ERR_ALIGNMENT, "attention: output offset %d not 16-byte aligned", i);
+    prm.out_delta[i] = ext.out_delta[i];
+  }
   const double sc = (scale > 0.f) ? (double)scale : 1.0 / std::sqrt((double)D);
   prm.scale_log2 = static_cast<float>(sc * 1.4426950408889634);
   prm.err = device_error_flag();
@@ -842,7 +899,7 @@ extern "C" int tm_attention_fwd(const void* q, int64_t q_batch_stride, int64_t q
   return attention_impl(q, q_batch_stride, q_row_stride, k_cache, v_cache, cache_batch_stride,
                         cache_row_stride, cache_rows, k_new, v_new, new_batch_stride,
                         new_row_stride, new_rows, spans, n_spans, out, out_batch_stride,
-                        out_row_stride, B, Lq, H, D, scale, nullptr, 0, stream);
+                        out_row_stride, B, Lq, H, D, scale, tm_attention_ext{}, stream);
 }
 
 extern "C" int tm_attention_fwd_ws(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
@@ -857,7 +914,8 @@ extern "C" int tm_attention_fwd_ws(const void* q, int64_t q_batch_stride, int64_
   return attention_impl(q, q_batch_stride, q_row_stride, k_cache, v_cache, cache_batch_stride,
                         cache_row_stride, cache_rows, k_new, v_new, new_batch_stride,
                         new_row_stride, new_rows, spans, n_spans, out, out_batch_stride,
-                        out_row_stride, B, Lq, H, D, scale, workspace, workspace_bytes, stream);
+                        out_row_stride, B, Lq, H, D, scale, ext_ws(workspace, workspace_bytes),
+                        stream);
 }
 
 extern "C" int64_t tm_attention_workspace_bytes(int B, int Lq, int H, int D,
@@ -900,8 +958,24 @@ extern "C" int tm_attention_fwd_dev_tiles(
   return attention_impl(q, q_batch_stride, q_row_stride, k_cache, v_cache, cache_batch_stride,
                         cache_row_stride, cache_rows, k_new, v_new, new_batch_stride,
                         new_row_stride, new_rows, spans, n_spans, out, out_batch_stride,
-                        out_row_stride, B, Lq, H, D, scale, workspace, workspace_bytes, stream,
-                        device_tiles);
+                        out_row_stride, B, Lq, H, D, scale,
+                        ext_ws(workspace, workspace_bytes, device_tiles), stream);
+}
+
+extern "C" int tm_attention_fwd_ext(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
+                                    const void* k_cache, const void* v_cache,
+                                    int64_t cache_batch_stride, int64_t cache_row_stride,
+                                    int64_t cache_rows, const void* k_new, const void* v_new,
+                                    int64_t new_batch_stride, int64_t new_row_stride,
+                                    int64_t new_rows, const tm_kv_span* spans, int n_spans,
+                                    void* out, int64_t out_batch_stride, int64_t out_row_stride,
+                                    int B, int Lq, int H, int D, float scale,
+                                    const tm_attention_ext* ext, void* stream) {
+  if (!ext) return set_error(TM_ERR_INVALID_ARGUMENT, "attention: null options");
+  return attention_impl(q, q_batch_stride, q_row_stride, k_cache, v_cache, cache_batch_stride,
+                        cache_row_stride, cache_rows, k_new, v_new, new_batch_stride,
+                        new_row_stride, new_rows, spans, n_spans, out, out_batch_stride,
+                        out_row_stride, B, Lq, H, D, scale, *ext, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -972,6 +1046,6 @@ extern "C" int tm_attention_fwd_noalloc(const void* q, int64_t q_batch_stride,
   return attention_impl(q, q_batch_stride, q_row_stride, k_cache, v_cache, cache_batch_stride,
                         cache_row_stride, cache_rows, k_new, v_new, new_batch_stride,
                         new_row_stride, new_rows, spans, n_spans, out, out_batch_stride,
-                        out_row_stride, B, Lq, H, D, scale, scratch, kNoAllocScratchBytes,
-                        stream);
+                        out_row_stride, B, Lq, H, D, scale,
+                        ext_ws(scratch, kNoAllocScratchBytes), stream);
 }

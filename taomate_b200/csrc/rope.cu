@@ -120,6 +120,7 @@ struct Job {
 struct NormRopeParams {
   Job jobs[kMaxJobs];
   int64_t row_begin[kMaxJobs + 1];  // prefix sums of B * L
+  int64_t delta[8];  // bytes from a job's output address to head group g's owner (peer store)
   int n_jobs;
   int B, H;
   float eps;
@@ -221,8 +222,10 @@ __global__ void __launch_bounds__(TPR) norm_rope_kernel(const __grid_constant__ 
     const uint4 v = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
                                pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
     const int g = h / Hl;
-    __nv_bfloat16* dst = jb.out + g * jb.ogs + b * jb.obs + l * jb.ors +
-                         static_cast<int64_t>(h - g * Hl) * D + j * 8;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(
+        reinterpret_cast<char*>(jb.out + g * jb.ogs + b * jb.obs + l * jb.ors +
+                                static_cast<int64_t>(h - g * Hl) * D + j * 8) +
+        p.delta[g]);
     *reinterpret_cast<uint4*>(dst) = v;
   }
 }
@@ -285,8 +288,8 @@ extern "C" int tm_rope_tables_split(void* cos_out, void* sin_out, int out_dtype,
   return check_cuda(cudaGetLastError(), "rope_tables: launch");
 }
 
-extern "C" int tm_norm_rope(const tm_norm_rope_job* jobs, int n_jobs, int B, int H, int D,
-                            float eps, int sp_size, void* stream) {
+static int norm_rope_impl(const tm_norm_rope_job* jobs, int n_jobs, int B, int H, int D,
+                          float eps, int sp_size, const int64_t* group_delta, void* stream) {
   using namespace tmb::rope;
   if (!jobs || n_jobs < 1 || n_jobs > kMaxJobs)
     return set_error(TM_ERR_INVALID_ARGUMENT, "norm_rope: %d jobs (1..%d)", n_jobs, kMaxJobs);
@@ -345,6 +348,14 @@ extern "C" int tm_norm_rope(const tm_norm_rope_job* jobs, int n_jobs, int B, int
     acc += static_cast<int64_t>(B) * j.L;
   }
   p.row_begin[n_jobs] = acc;
+  if (group_delta) {
+    if (sp_size > 8) return set_error(TM_ERR_UNSUPPORTED, "norm_rope: more than 8 peer groups");
+    for (int g = 0; g < sp_size; ++g) {
+      if (group_delta[g] & 15)
+        return set_error(TM_ERR_ALIGNMENT, "norm_rope: peer offset %d not 16-byte aligned", g);
+      p.delta[g] = group_delta[g];
+    }
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (inner) {  // chunks per thread x threads per row = inner / 8
     case 256: return D == 128 ? launch_norm_rope<128, 1, 32>(p, s) : launch_norm_rope<64, 1, 32>(p, s);
@@ -355,4 +366,16 @@ extern "C" int tm_norm_rope(const tm_norm_rope_job* jobs, int n_jobs, int B, int
     default: break;
   }
   return set_error(TM_ERR_UNSUPPORTED, "norm_rope: H*D=%d not built", inner);
+}
+
+extern "C" int tm_norm_rope(const tm_norm_rope_job* jobs, int n_jobs, int B, int H, int D,
+                            float eps, int sp_size, void* stream) {
+  return norm_rope_impl(jobs, n_jobs, B, H, D, eps, sp_size, nullptr, stream);
+}
+
+extern "C" int tm_norm_rope_peer(const tm_norm_rope_job* jobs, int n_jobs, int B, int H, int D,
+                                 float eps, int sp_size, const int64_t* group_delta,
+                                 void* stream) {
+  if (!group_delta) return set_error(TM_ERR_INVALID_ARGUMENT, "norm_rope_peer: null offsets");
+  return norm_rope_impl(jobs, n_jobs, B, H, D, eps, sp_size, group_delta, stream);
 }

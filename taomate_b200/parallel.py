@@ -16,6 +16,11 @@ B200 design:
   the exchange Q/K/V are strided views with a uniform row stride that the
   attention kernel's TMA maps read directly.
 
+With :func:`init_peer_exchange` the two exchanges of ``attention_with_cache``
+skip NCCL: every rank maps its peers' receive buffers (CUDA IPC) and the
+producing kernels store rows straight into the owner's buffer over NVLink,
+followed by a bounded flag handshake (:class:`PeerExchange`).
+
 Layout permutes run on CUDA tensors only.  A test may register a
 permute implementation for another device type (e.g. CPU ranks on gloo)
 with :func:`register_layout_copy`; the library registers none.
@@ -385,3 +390,137 @@ def gather_sequence(x: torch.Tensor, dim: int = 1, group=None, sp_size: Optional
     parts = [torch.empty_like(x) for _ in range(sp_size)]
     dist.all_gather(parts, x, group=group)
     return torch.cat(parts, dim=dim)
+
+
+# ---------------------------------------------------------------------------
+# Fused exchanges over NVLink peer memory
+# ---------------------------------------------------------------------------
+class _DevBuffer:
+    """A cudaMalloc'd buffer exposed to torch without a copy."""
+
+    def __init__(self, ptr: int, nbytes: int, device: torch.device):
+        self.__cuda_array_interface__ = {"shape": (nbytes // 2,), "typestr": "<u2",
+                                         "data": (ptr, False), "version": 3, "strides": None}
+        self.tensor = torch.as_tensor(self, device=device).view(torch.bfloat16)
+
+
+class PeerExchange:
+    """Receive buffers of the two Ulysses exchanges, mapped on every rank.
+
+    * ``recv``: ``[sp, B, S_loc, 3, H/sp, D]`` — Q, K, V of the full chunk for
+      this rank's heads; rank g's norm+RoPE kernel stores its tokens at
+      ``recv[g]`` (all_to_all.py:125-151 layout).
+    * ``out``: ``[B, S_loc, H, D]`` — this rank's tokens for all heads; rank
+      g's attention kernel stores heads ``g * H/sp ...`` of them
+      (all_to_all.py:154-173).
+    * flags and device epoch counters for the handshakes (slot 0: seq->head,
+      slot 1: head->seq).
+
+    The buffers are reused by every call: the returned Q/K/V/out are views
+    that the next call overwrites (``attention_with_cache`` copies the new K/V
+    it returns).  One exchange object per process; calls must come in the
+    same order on every rank.
+    """
+
+    def __init__(self, group, sp_size: int, rank: int, batch: int, tokens_local: int,
+                 heads: int, dim_head: int, device: torch.device):
+        if sp_size < 2 or sp_size > 8 or heads % sp_size:
+            raise ValueError(f"peer exchange needs 2..8 ranks dividing {heads} heads")
+        lib = _lib.load()
+        self.lib, self.group, self.sp, self.rank = lib, group, sp_size, rank
+        self.B, self.S_loc, self.H, self.D = batch, tokens_local, heads, dim_head
+        self.Hl = heads // sp_size
+        self.device = torch.device(device)
+        el = 2
+        sizes = {
+            "recv": sp_size * batch * tokens_local * 3 * self.Hl * dim_head * el,
+            "out": batch * tokens_local * heads * dim_head * el,
+            "flags": int(lib.tm_peer_flag_bytes()),
+        }
+        self._own: Dict[str, int] = {}
+        self._opened = []
+        handles = {}
+        with torch.cuda.device(self.device):
+            for name, n in sizes.items():
+                ptr = ctypes.c_void_p()
+                h = (ctypes.c_char * 64)()
+                _lib.check(lib.tm_peer_alloc(n, ctypes.byref(ptr), ctypes.cast(h, ctypes.c_void_p)),
+                           "peer_alloc")
+                self._own[name] = int(ptr.value)
+                handles[name] = bytes(h)
+            gathered = [None] * sp_size
+            dist.all_gather_object(gathered, handles, group=group)
+            self.peers: Dict[str, list] = {name: [] for name in sizes}
+            for g in range(sp_size):
+                for name in sizes:
+                    if g == rank:
+                        self.peers[name].append(self._own[name])
+                        continue
+                    p = ctypes.c_void_p()
+                    hb = (ctypes.c_char * 64).from_buffer_copy(gathered[g][name])
+                    _lib.check(lib.tm_peer_open(ctypes.cast(hb, ctypes.c_void_p), ctypes.byref(p)),
+                               "peer_open")
+                    self.peers[name].append(int(p.value))
+                    self._opened.append(int(p.value))
+        self.delta = {name: (ctypes.c_int64 * 8)(*[v - self._own[name] for v in self.peers[name]])
+                      for name in ("recv", "out")}
+        self._flag_ptrs = (ctypes.c_void_p * 8)(*self.peers["flags"])
+        self._counters = self._own["flags"] + sizes["flags"] - 64
+        self.recv = _DevBuffer(self._own["recv"], sizes["recv"], self.device).tensor.view(
+            sp_size, batch, tokens_local, 3, self.Hl, dim_head)
+        self.out = _DevBuffer(self._own["out"], sizes["out"], self.device).tensor.view(
+            batch, tokens_local, heads, dim_head)
+
+    def fits(self, B: int, L: int, H: int, D: int) -> bool:
+        return (B, L, H, D) == (self.B, self.S_loc, self.H, self.D)
+
+    def exchange(self, slot: int) -> None:
+        """Publish this rank's stores of ``slot`` and wait for every rank's."""
+        stream = _lib.stream_ptr(self.device)
+        _lib.check(self.lib.tm_peer_signal(self._flag_ptrs, self.sp, self.rank, self._counters,
+                                           slot, stream), "peer_signal")
+        _lib.check(self.lib.tm_peer_wait(self._own["flags"], self.sp, self._counters, slot,
+                                         stream), "peer_wait")
+        _lib.launched(2)
+
+    def close(self) -> None:
+        if not self._own:
+            return
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                self.lib.tm_peer_close(ctypes.c_void_p(p))
+            for p in self._own.values():
+                self.lib.tm_peer_free(ctypes.c_void_p(p))
+        self._opened, self._own = [], {}
+
+
+_PEER: Optional[PeerExchange] = None
+
+
+def init_peer_exchange(batch: int, tokens_local: int, heads: int, dim_head: int,
+                       device=None) -> Optional[PeerExchange]:
+    """Map NVLink receive buffers for ``attention_with_cache``'s exchanges on
+    the SP group (collective over the group; call after :func:`init_sp_mesh`
+    on every rank).  Calls whose shapes differ keep using NCCL."""
+    global _PEER
+    if not is_sp_enabled():
+        return None
+    if _PEER is not None:
+        _PEER.close()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    _PEER = PeerExchange(_SP_GROUP, _SP_SIZE, _SP_RANK, batch, tokens_local, heads, dim_head,
+                         dev)
+    return _PEER
+
+
+def get_peer_exchange() -> Optional[PeerExchange]:
+    return _PEER
+
+
+def close_peer_exchange() -> None:
+    """Unmap and free the exchange buffers (before the process group goes)."""
+    global _PEER
+    if _PEER is not None:
+        _PEER.close()
+    _PEER = None

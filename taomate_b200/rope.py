@@ -131,7 +131,7 @@ def _pe_strides(cos: torch.Tensor) -> Tuple[int, int, int]:
 
 
 def norm_rope(xs, weights, pes, heads: int, dim_head: int, eps: float, sp_size: int = 1,
-              packed: bool = False):
+              packed: bool = False, peer=None):
     """Fused RMSNorm + split RoPE over up to four ``[B, L, H*D]`` bf16 tensors
     in one launch (weight ``None`` skips the norm, pe ``None`` skips the
     rotation, both ``None`` is a layout copy).
@@ -140,14 +140,21 @@ def norm_rope(xs, weights, pes, heads: int, dim_head: int, eps: float, sp_size: 
     ``sp_size > 1``: the store writes the Ulysses seq->head send layout.  With
     ``packed=True`` all jobs share one buffer ``[sp, B, L, n, H/sp, D]`` (job
     ``j`` at index ``j`` of dim 3), which is returned alone; otherwise each job
-    gets its own ``[sp, B, L, H/sp, D]`` buffer.
+    gets its own ``[sp, B, L, H/sp, D]`` buffer.  With ``peer`` (a
+    :class:`taomate_b200.parallel.PeerExchange`, packed jobs only) the kernel
+    stores head group g straight into rank g's receive buffer, at this rank's
+    slot; the caller then runs ``peer.exchange(0)`` and reads ``peer.recv``.
     """
     dev = _lib.require_cuda(*xs)
     B = int(xs[0].shape[0])
     n = len(xs)
     Hl = heads // sp_size
     L0 = int(xs[0].shape[1])
-    if packed:
+    if peer is not None:
+        if not packed or n != 3 or not peer.fits(B, L0, heads, dim_head) or sp_size != peer.sp:
+            raise ValueError("peer stores need the exchange's packed Q/K/V shapes")
+        buf = peer.recv
+    elif packed:
         if any(int(x.shape[1]) != L0 for x in xs):
             raise ValueError("packed send buffer needs equal lengths")
         buf = torch.empty(sp_size, B, L0, n, Hl, dim_head, device=dev, dtype=torch.bfloat16)
@@ -161,7 +168,11 @@ def norm_rope(xs, weights, pes, heads: int, dim_head: int, eps: float, sp_size: 
             raise ValueError(f"expected [B, L, {heads * dim_head}] rows, got {tuple(x.shape)}")
         L = int(x.shape[1])
         j = jobs[i]
-        if packed:
+        if peer is not None:
+            o = buf[peer.rank, :, :, i]  # this rank's slot; group g adds rank g's offset
+            j.out = o.data_ptr()
+            j.out_group_stride, j.out_batch_stride, j.out_row_stride = 0, buf.stride(1), buf.stride(2)
+        elif packed:
             o = buf[:, :, :, i]
             j.out = o.data_ptr()
             j.out_group_stride, j.out_batch_stride, j.out_row_stride = buf.stride(0), buf.stride(1), buf.stride(2)
@@ -200,8 +211,13 @@ def norm_rope(xs, weights, pes, heads: int, dim_head: int, eps: float, sp_size: 
         j.L = L
     lib = _lib.load()
     with torch.cuda.device(dev):
-        _lib.check(lib.tm_norm_rope(jobs, n, B, int(heads), int(dim_head), float(eps),
-                                    int(sp_size), _lib.stream_ptr(dev)), "norm_rope")
+        if peer is not None:
+            _lib.check(lib.tm_norm_rope_peer(jobs, n, B, int(heads), int(dim_head), float(eps),
+                                             int(sp_size), peer.delta["recv"],
+                                             _lib.stream_ptr(dev)), "norm_rope")
+        else:
+            _lib.check(lib.tm_norm_rope(jobs, n, B, int(heads), int(dim_head), float(eps),
+                                        int(sp_size), _lib.stream_ptr(dev)), "norm_rope")
         _lib.launched()
     return buf if packed else outs
 

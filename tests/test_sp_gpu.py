@@ -35,8 +35,10 @@ def _free_port():
 
 def _worker(rank, world, port, outdir):
     sys.path.insert(0, os.path.dirname(HERE))
+    import ctypes
+
     import taomate_b200 as tm
-    from taomate_b200 import parallel as P
+    from taomate_b200 import _lib, parallel as P
     from taomate_b200.attention import AttentionWeights
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -70,10 +72,26 @@ def _worker(rank, world, port, outdir):
             out, nk, nv = tm.attention_with_cache(
                 attn, x[:, ts].contiguous(), None, (cos[:, :, ts], sin[:, :, ts]), None,
                 ck[:, :, hs].contiguous(), cv[:, :, hs].contiguous())
+        # the same calls with the exchanges fused into the kernels' NVLink stores,
+        # twice in a row (the second on other inputs: buffers and flag epochs reused)
+        P.init_peer_exchange(1, sl, heads, dim_head)
+        x2 = torch.randn(1, lq, hidden, device=dev, generator=g).to(torch.bfloat16)
+        with torch.no_grad():
+            out_p, nk_p, nv_p = tm.attention_with_cache(
+                attn, x[:, ts].contiguous(), None, (cos[:, :, ts], sin[:, :, ts]), None,
+                ck[:, :, hs].contiguous(), cv[:, :, hs].contiguous())
+            out_p = out_p.clone()
+            out_p2, _, _ = tm.attention_with_cache(
+                attn, x2[:, ts].contiguous(), None, (cos[:, :, ts], sin[:, :, ts]), None,
+                ck[:, :, hs].contiguous(), cv[:, :, hs].contiguous())
         torch.cuda.synchronize()
+        code = ctypes.c_int(0)
+        assert _lib.load().tm_device_error(ctypes.byref(code)) == 0 and code.value == 0
+        P.close_peer_exchange()
         f = lambda t: t.float().cpu().numpy()
         np.savez(os.path.join(outdir, f"r{rank}.npz"), out=f(out), ref_out=f(ref_out[:, ts]),
-                 k=f(nk), ref_k=f(ref_k[:, :, hs]), v=f(nv), ref_v=f(ref_v[:, :, hs]))
+                 k=f(nk), ref_k=f(ref_k[:, :, hs]), v=f(nv), ref_v=f(ref_v[:, :, hs]),
+                 out_p=f(out_p), k_p=f(nk_p), v_p=f(nv_p), out_p2=f(out_p2))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -98,3 +116,7 @@ def test_ulysses_sp2_matches_single_gpu(tmp_path):
         assert _rel_l2(z["k"], z["ref_k"]) < 5e-3
         assert _rel_l2(z["v"], z["ref_v"]) < 5e-3
         assert _rel_l2(z["out"], z["ref_out"]) < 1e-2
+        # fused NVLink exchanges: the same kernels and data as the NCCL path
+        assert _rel_l2(z["out_p"], z["out"]) < 1e-3
+        assert _rel_l2(z["k_p"], z["k"]) < 1e-3 and _rel_l2(z["v_p"], z["v"]) < 1e-3
+        assert _rel_l2(z["out_p2"], z["out_p"]) > 1e-1  # the second call saw new inputs
