@@ -1,4 +1,4 @@
-"""Ulysses sequence parallelism over NCCL on 2 GPUs (skipped with fewer).
+"""Ulysses sequence parallelism on 2, 4 and 8 GPUs (each skipped with fewer).
 
 Each rank holds its shard of the chunk's tokens and a head shard of the KV
 cache over the whole sequence, as the reference lays them out
@@ -22,7 +22,6 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-WORLD = 2
 
 
 def _free_port():
@@ -104,10 +103,12 @@ def _rel_l2(a, b):
 
 
 @pytest.mark.gpu
-@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-def test_ulysses_sp2_matches_single_gpu(tmp_path):
-    mp.spawn(_worker, args=(WORLD, _free_port(), str(tmp_path)), nprocs=WORLD, join=True)
-    for r in range(WORLD):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ulysses_sp_matches_single_gpu(tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
         z = np.load(tmp_path / f"r{r}.npz")
         assert z["out"].shape == z["ref_out"].shape
         assert z["k"].shape == z["ref_k"].shape
