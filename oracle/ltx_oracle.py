@@ -295,6 +295,44 @@ def attention_with_cache(x: np.ndarray, params: Dict[str, np.ndarray], heads: in
     return out, k, v
 
 
+def text_cross_attention(x: np.ndarray, context: np.ndarray, params: Dict[str, np.ndarray],
+                         heads: int, dim_head: int, mask: Optional[np.ndarray] = None,
+                         eps: float = 1e-6, dtype=np.float64) -> np.ndarray:
+    """Text cross-attention with cached K/V projections
+    (``_text_cross_attention_with_kv_cache``, ltx_causal/transformer/kv_cache.py:764-827;
+    the cache only skips recomputing K/V).
+
+    ``x``: ``[B, Lq, Dq]``, ``context``: ``[B, Lk, Dc]``, ``mask``: ``[B, Lk]``
+    0/1 (1 = real token) turned into the additive ``(mask - 1) * float32 max``
+    of ``_prepare_attention_mask`` (ltx_causal/transformer/causal_model.py:551-562).
+    Steps: q = q_norm(to_q(x)) (:796), k = k_norm(to_k(context)), v = to_v(context)
+    (:744-747), SDPA with the mask (:811, flex_attention_utils.py:245-276), gate
+    2·sigmoid(to_gate_logits(x)) (:821-825), to_out (:826).  No RoPE.
+    """
+    f = lambda a: np.asarray(a, dtype=dtype)
+    B = x.shape[0]
+    outs = []
+    for b in range(B):
+        q = rms_norm(f(x[b]) @ f(params["to_q_w"]).T + f(params["to_q_b"]), params["q_norm_w"], eps)
+        k = rms_norm(f(context[b]) @ f(params["to_k_w"]).T + f(params["to_k_b"]),
+                     params["k_norm_w"], eps)
+        v = f(context[b]) @ f(params["to_v_w"]).T + f(params["to_v_b"])
+        q = q.reshape(q.shape[0], heads, dim_head)
+        k = k.reshape(k.shape[0], heads, dim_head)
+        v = v.reshape(v.shape[0], heads, dim_head)
+        add = None
+        if mask is not None:
+            row = (f(mask[b]) - 1.0) * float(np.finfo(np.float32).max)
+            add = np.broadcast_to(row[None, :], (q.shape[0], k.shape[0]))
+        o = attention(q, k, v, mask=add, dtype=dtype).reshape(q.shape[0], heads * dim_head)
+        if "to_gate_logits_w" in params:
+            g = f(x[b]) @ f(params["to_gate_logits_w"]).T + f(params["to_gate_logits_b"])
+            gates = 2.0 / (1.0 + np.exp(-g))
+            o = (o.reshape(-1, heads, dim_head) * gates[:, :, None]).reshape(o.shape)
+        outs.append(o @ f(params["to_out_w"]).T + f(params["to_out_b"]))
+    return np.stack(outs)
+
+
 # ----------------------------------------------------------------------------
 # A4 / A8 / A13: Ulysses layout permutations (global view over all ranks)
 # ----------------------------------------------------------------------------

@@ -135,11 +135,177 @@ def _workspace_bytes(lib, dev, B, Lq, H, D, keys) -> int:
 
 def standard_attention_forward(q: Tensor, k: Tensor, v: Tensor, mask: Optional[Tensor] = None,
                                scale: Optional[float] = None) -> Tensor:
-    """Unmasked SDPA on ``[B, L, H, D]`` tensors (flex_attention_utils.py:225-276)."""
-    if mask is not None:
-        raise NotImplementedError("masked attention is not on the streaming path; "
-                                  "the KV-cache path calls this with mask=None")
-    return flash_attention(q, None, None, (), k, v, int(k.shape[1]), scale)
+    """SDPA on ``[B, L, H, D]`` tensors (flex_attention_utils.py:225-276).
+
+    ``mask`` may be a key-padding mask (see :func:`key_padding_runs`): the
+    visible keys become the kernel's key spans.  Other masks (per-query
+    patterns, non-binary biases) raise ``NotImplementedError``."""
+    if mask is None:
+        return flash_attention(q, None, None, (), k, v, int(k.shape[1]), scale)
+    B, Lk = int(q.shape[0]), int(k.shape[1])
+    return _masked_attention(q, k, v, key_padding_runs(mask, B, Lk), scale)
+
+
+_RUNS_CACHE: "OrderedDict" = None
+
+
+def key_padding_runs(mask: Tensor, batch: int, kv_len: int):
+    """Per batch element, the runs ``[(start, rows), ...]`` of visible keys of
+    a key-padding mask: boolean / integer ``[B, Lk]`` or ``[B, 1, 1, Lk]``
+    (True / 1 = visible, as SDPA's boolean masks), or the additive float mask
+    of ``_prepare_attention_mask`` (ltx_causal/transformer/causal_model.py:
+    551-562: 0 visible, ``-finfo.max`` padding; ``[B, 1, 1, Lk]``, or
+    ``[B, 1, Lq, Lk]`` with equal rows).  One device-to-host read per mask
+    tensor (cached by identity and version)."""
+    global _RUNS_CACHE
+    from collections import OrderedDict
+    if _RUNS_CACHE is None:
+        _RUNS_CACHE = OrderedDict()
+    key = (mask.data_ptr(), mask._version, tuple(mask.shape), str(mask.dtype), batch, kv_len)
+    hit = _RUNS_CACHE.get(key)
+    if hit is not None:
+        _RUNS_CACHE.move_to_end(key)
+        return hit
+    m = mask.detach()
+    if m.dim() == 2:
+        m = m[:, None, None, :]
+    elif m.dim() == 3:
+        m = m[:, None]
+    if m.dim() != 4 or m.shape[-1] != kv_len or m.shape[1] != 1 or m.shape[0] not in (1, batch):
+        raise NotImplementedError(f"only key-padding masks are supported, got {tuple(mask.shape)}")
+    m = m.to("cpu")
+    if m.dtype == torch.bool:
+        vis = m
+    elif not torch.is_floating_point(m):
+        vis = m != 0
+    else:
+        big = torch.finfo(m.dtype).max
+        vis = m == 0
+        if not bool(((m == 0) | (m <= -big * 0.5) | torch.isinf(m)).all()):
+            raise NotImplementedError("additive masks other than 0 / -max are not supported")
+    if vis.shape[2] > 1 and not bool((vis == vis[:, :, :1]).all()):
+        raise NotImplementedError("per-query masks are not supported (key padding only)")
+    vis = vis[:, 0, 0].expand(batch, kv_len)
+    runs = []
+    for b in range(batch):
+        row = vis[b].tolist()
+        r, i = [], 0
+        while i < kv_len:
+            if row[i]:
+                j = i
+                while j < kv_len and row[j]:
+                    j += 1
+                r.append((i, j - i))
+                i = j
+            else:
+                i += 1
+        runs.append(r)
+    _RUNS_CACHE[key] = runs
+    while len(_RUNS_CACHE) > 64:
+        _RUNS_CACHE.popitem(last=False)
+    return runs
+
+
+def _masked_attention(q: Tensor, k: Tensor, v: Tensor, runs, scale: Optional[float] = None,
+                      out: Optional[Tensor] = None) -> Tensor:
+    """Attention of ``q`` over the key runs of each batch element (one launch
+    when every element has the same runs).  An element without visible keys
+    gets the mean of V over all keys — what the additive ``-finfo.max`` mask
+    gives once every score saturates to the same value."""
+    B, Lq, H, D = (int(t) for t in q.shape)
+    if out is None:
+        out = torch.empty(B, Lq, H, D, device=q.device, dtype=q.dtype)
+    if all(r == runs[0] for r in runs) and runs[0]:
+        return flash_attention(q, k, v, runs[0], None, None, 0, scale, out=out)
+    for b in range(B):
+        if runs[b]:
+            flash_attention(q[b:b + 1], k[b:b + 1], v[b:b + 1], runs[b], None, None, 0, scale,
+                            out=out[b:b + 1])
+        else:
+            out[b] = v[b].float().mean(dim=0, keepdim=True).to(out.dtype).expand(Lq, H, D)
+    return out
+
+
+def _text_kv(attn, context: Tensor, base_context: Tensor, prompt_cache_key, cache_name: str,
+             sp_size: int) -> Tuple[Tensor, Tensor]:
+    """k_norm(to_k(context)) and to_v(context) as ``[B, Lk, H(/sp), D]``, with
+    the reference's exact inference LRU (kv_cache.py:676-761): keyed by the
+    module, the identity / pointer / shape of ``base_context``, the prompt key
+    and the SP rank; 4 entries per module; an entry is valid only while
+    ``base_context`` is the same live object."""
+    import weakref
+    from collections import OrderedDict
+    H, D = int(attn.heads), int(attn.dim_head)
+    B = int(context.shape[0])
+    key = None
+    try:
+        weakref.ref(base_context)
+        rank = P.get_sp_rank() if sp_size > 1 else 0
+        key = (cache_name, id(attn), id(base_context), int(base_context.data_ptr()),
+               tuple(base_context.shape), tuple(base_context.stride()), str(base_context.dtype),
+               str(base_context.device), prompt_cache_key, tuple(context.shape),
+               str(context.dtype), str(context.device), int(sp_size), int(rank))
+    except TypeError:
+        key = None
+    cache = getattr(attn, "_ltx_text_cross_kv_cache", None)
+    if key is not None:
+        if cache is None:
+            cache = OrderedDict()
+            setattr(attn, "_ltx_text_cross_kv_cache", cache)
+        hit = cache.get(key)
+        if hit is not None:
+            ref, k, v = hit
+            if ref() is base_context:
+                cache.move_to_end(key)
+                return k, v
+            cache.pop(key, None)
+    k = F.linear(context, attn.to_k.weight, attn.to_k.bias)
+    (k,) = norm_rope([k], [attn.k_norm.weight], [None], H, D, _norm_eps(attn.k_norm))
+    v = F.linear(context, attn.to_v.weight, attn.to_v.bias).view(B, -1, H, D)
+    if sp_size > 1:
+        Hl = H // sp_size
+        h0 = P.get_sp_rank() * Hl
+        k = k.narrow(2, h0, Hl).contiguous()
+        v = v.narrow(2, h0, Hl).contiguous()
+    if key is not None:
+        cache[key] = (weakref.ref(base_context), k, v)
+        cache.move_to_end(key)
+        while len(cache) > 4:
+            cache.popitem(last=False)
+    return k, v
+
+
+def text_cross_attention_with_kv_cache(attn, x: Tensor, context: Tensor, *,
+                                       mask: Optional[Tensor], base_context: Tensor,
+                                       prompt_cache_key=None, cache_name: str = "text",
+                                       layer_idx: Optional[int] = None) -> Tensor:
+    """Text cross-attention with cached K/V projections
+    (``_text_cross_attention_with_kv_cache``, kv_cache.py:764-827): video
+    queries against a prompt's text tokens; the padding mask becomes the
+    kernel's key spans (no mask tensor is built), K/V projections are cached
+    per prompt as the reference does, Q goes through seq->head under SP and
+    the output back through head->seq, then gate and out projection."""
+    B = int(x.shape[0])
+    H, D = int(attn.heads), int(attn.dim_head)
+    sp_size = P.get_sp_world_size() if P.is_sp_enabled() else 1
+    with section(f"{cache_name}.text_q_project"):
+        q = F.linear(x, attn.to_q.weight, attn.to_q.bias)
+        (q,) = norm_rope([q], [attn.q_norm.weight], [None], H, D, _norm_eps(attn.q_norm))
+        if sp_size > 1:
+            q = P.seq_all_to_all_head(q, P.get_sp_group(), sp_size)
+    k, v = _text_kv(attn, context, base_context, prompt_cache_key, cache_name, sp_size)
+    runs = [[(0, int(k.shape[1]))]] * B if mask is None else key_padding_runs(mask, B,
+                                                                            int(k.shape[1]))
+    with section(f"{cache_name}.text_sdpa"):
+        out = _masked_attention(q, k, v, runs)
+    if sp_size > 1:
+        with section(f"{cache_name}.text_a2a_head2seq"):
+            out = P.head_all_to_all_seq(out, P.get_sp_group(), sp_size)
+    out = out.reshape(B, -1, H * D)
+    if getattr(attn, "to_gate_logits", None) is not None:
+        gates = 2.0 * torch.sigmoid(attn.to_gate_logits(x))
+        out = (out.view(B, -1, H, D) * gates.unsqueeze(-1)).view(B, -1, H * D)
+    return attn.to_out(out)
 
 
 def _norm_eps(norm) -> float:
@@ -157,6 +323,49 @@ def _cache_source(cached_k, cached_v):
         kt, rows = cache_rows_view(cached_k)
         return kt, cached_k.arena.v, rows
     return cached_k, cached_v, [(0, int(cached_k.shape[1]))]
+
+
+_SIDE_STREAMS = {}
+
+
+def _linear_into(out2d: Tensor, x: Tensor, lin) -> None:
+    x2d = x.reshape(-1, x.shape[-1])
+    if lin.bias is not None:
+        torch.addmm(lin.bias, x2d, lin.weight.t(), out=out2d)
+    else:
+        torch.mm(x2d, lin.weight.t(), out=out2d)
+
+
+def _projections(attn, x: Tensor, ctx: Tensor):
+    """q, k, v projections.  While a CUDA graph is being captured and the
+    chunk is short (a sequence-parallel shard), k and v run on two side
+    streams next to q: one 144-row GEMM fills a fraction of the SMs, three
+    side by side fill more, at no cost when the graph replays."""
+    if not (x.is_cuda and x.shape[1] <= 576 and torch.cuda.is_current_stream_capturing()):
+        return (F.linear(x, attn.to_q.weight, attn.to_q.bias),
+                F.linear(ctx, attn.to_k.weight, attn.to_k.bias),
+                F.linear(ctx, attn.to_v.weight, attn.to_v.bias))
+    dev = x.device
+    side = _SIDE_STREAMS.get(dev.index)
+    if side is None:
+        side = _SIDE_STREAMS[dev.index] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    main = torch.cuda.current_stream(dev)
+    B = x.shape[0]
+    # outputs allocated on the main stream, which joins the side streams
+    # before anything reads or frees them
+    q = torch.empty(B, x.shape[1], attn.to_q.weight.shape[0], device=dev, dtype=x.dtype)
+    k = torch.empty(B, ctx.shape[1], attn.to_k.weight.shape[0], device=dev, dtype=x.dtype)
+    v = torch.empty(B, ctx.shape[1], attn.to_v.weight.shape[0], device=dev, dtype=x.dtype)
+    for st in side:
+        st.wait_stream(main)
+    with torch.cuda.stream(side[0]):
+        _linear_into(k.view(-1, k.shape[-1]), ctx, attn.to_k)
+    with torch.cuda.stream(side[1]):
+        _linear_into(v.view(-1, v.shape[-1]), ctx, attn.to_v)
+    _linear_into(q.view(-1, q.shape[-1]), x, attn.to_q)
+    for st in side:
+        main.wait_stream(st)
+    return q, k, v
 
 
 def attention_with_cache(
@@ -194,9 +403,7 @@ def attention_with_cache(
         raise NotImplementedError("text cross-attention (replicated K/V) is not on this path")
 
     # 1. projections (library GEMMs)
-    q = F.linear(x, attn.to_q.weight, attn.to_q.bias)
-    k = F.linear(ctx, attn.to_k.weight, attn.to_k.bias)
-    v = F.linear(ctx, attn.to_v.weight, attn.to_v.bias)
+    q, k, v = _projections(attn, x, ctx)
     q_pe = pe
     kk_pe = k_pe if k_pe is not None else pe
     eps_q, eps_k = _norm_eps(attn.q_norm), _norm_eps(attn.k_norm)

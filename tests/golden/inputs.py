@@ -64,6 +64,44 @@ def attn_case_inputs(name: str) -> dict:
     return dict(cfg=c, params=p, x=x, cached_k=ck, cached_v=cv)
 
 
+# Text cross-attention (kv_cache.py:764-827): video queries against a padded
+# text context; per-batch key-padding masks as _prepare_attention_mask builds them.
+TEXT_CROSS_CASES: Dict[str, dict] = {
+    "plain": dict(hidden=256, ctx_dim=384, heads=4, dim_head=64, lq=96, lk=48, batch=2,
+                  valid=(40, 48), gated=False, seed=10),
+    "gated": dict(hidden=256, ctx_dim=384, heads=4, dim_head=64, lq=96, lk=48, batch=1,
+                  valid=(33,), gated=True, seed=11),
+    "d128": dict(hidden=512, ctx_dim=256, heads=4, dim_head=128, lq=130, lk=70, batch=1,
+                 valid=(70,), gated=False, seed=12),
+}
+
+
+def text_cross_inputs(name: str) -> dict:
+    """Seeded inputs of a text cross-attention case: weights ([out, in]),
+    x ``[B, lq, hidden]``, context ``[B, lk, ctx_dim]`` and the 0/1 key mask
+    ``[B, lk]`` (valid keys first, then padding)."""
+    c = TEXT_CROSS_CASES[name]
+    rng = np.random.default_rng(2000 + c["seed"])
+    hid, ctx, inner = c["hidden"], c["ctx_dim"], c["heads"] * c["dim_head"]
+    p = {}
+    for nm, (o, i) in {"to_q": (inner, hid), "to_k": (inner, ctx), "to_v": (inner, ctx),
+                       "to_out": (hid, inner)}.items():
+        p[nm + "_w"] = (rng.standard_normal((o, i)) * 0.02).astype(np.float32)
+        p[nm + "_b"] = (rng.standard_normal(o) * 0.02).astype(np.float32)
+    if c["gated"]:
+        p["to_gate_logits_w"] = (rng.standard_normal((c["heads"], hid)) * 0.02).astype(np.float32)
+        p["to_gate_logits_b"] = (rng.standard_normal(c["heads"]) * 0.02).astype(np.float32)
+    p["q_norm_w"] = rng.uniform(0.5, 1.5, inner).astype(np.float32)
+    p["k_norm_w"] = rng.uniform(0.5, 1.5, inner).astype(np.float32)
+    B = c["batch"]
+    x = rng.standard_normal((B, c["lq"], hid)).astype(np.float32)
+    context = rng.standard_normal((B, c["lk"], ctx)).astype(np.float32)
+    mask = np.zeros((B, c["lk"]), np.int64)
+    for b, n in enumerate(c["valid"]):
+        mask[b, :n] = 1
+    return dict(cfg=c, params=p, x=x, context=context, mask=mask)
+
+
 def split_rope_inputs() -> np.ndarray:
     """x ``[96, 256]`` for the split-RoPE case (C1 shapes)."""
     return np.random.default_rng(77).standard_normal((96, 256)).astype(np.float32)

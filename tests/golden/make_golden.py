@@ -123,6 +123,43 @@ def _attn_case(causal_rope, CausalLTXAttention, kv_cache, torch, name):
     np.savez_compressed(os.path.join(HERE, f"attn_{name}.npz"), **rec)
 
 
+def gen_text_cross(CausalLTXAttention, kv_cache, torch):
+    """_text_cross_attention_with_kv_cache (kv_cache.py:764-827) with the
+    K/V cache switched on, the mask prepared as causal_model.py:551-562 does,
+    called twice (miss, then cache hit) in fp32 and bf16."""
+    kv_cache._CACHE_TEXT_CROSS_KV = True
+    for name in inputs.TEXT_CROSS_CASES:
+        d = inputs.text_cross_inputs(name)
+        c, prm = d["cfg"], d["params"]
+        attn = CausalLTXAttention(c["hidden"], c["ctx_dim"], heads=c["heads"],
+                                  dim_head=c["dim_head"], apply_gated_attention=c["gated"])
+        attn.eval()
+        with torch.no_grad():
+            mods = {"to_q": attn.to_q, "to_k": attn.to_k, "to_v": attn.to_v,
+                    "to_out": attn.to_out[0]}
+            if c["gated"]:
+                mods["to_gate_logits"] = attn.to_gate_logits
+            for nm, m in mods.items():
+                m.weight.copy_(torch.from_numpy(prm[nm + "_w"]))
+                m.bias.copy_(torch.from_numpy(prm[nm + "_b"]))
+            attn.q_norm.weight.copy_(torch.from_numpy(prm["q_norm_w"]))
+            attn.k_norm.weight.copy_(torch.from_numpy(prm["k_norm_w"]))
+        rec = {}
+        for tag, dt in (("f32", torch.float32), ("bf16", torch.bfloat16)):
+            a = attn.to(dt)
+            x = torch.from_numpy(d["x"]).to(dt)
+            ctx = torch.from_numpy(d["context"]).to(dt)
+            m = torch.from_numpy(d["mask"])
+            mask = (m - 1).to(dt).reshape(m.shape[0], 1, -1, m.shape[-1]) * torch.finfo(dt).max
+            with torch.no_grad():
+                outs = [kv_cache._text_cross_attention_with_kv_cache(
+                    a, x, ctx, mask=mask, base_context=ctx, prompt_cache_key=None,
+                    cache_name="text", layer_idx=0) for _ in range(2)]
+            assert torch.equal(outs[0], outs[1])
+            rec[f"out_{tag}"] = f32(outs[0])
+        np.savez_compressed(os.path.join(HERE, f"text_cross_{name}.npz"), **rec)
+
+
 def gen_attention(causal_rope, CausalLTXAttention, kv_cache, torch):
     for name in inputs.ATTN_CASES:
         _attn_case(causal_rope, CausalLTXAttention, kv_cache, torch, name)
@@ -238,6 +275,7 @@ def main():
     gen_rope(causal_rope, torch)
     gen_split_rope(causal_rope, torch)
     gen_attention(causal_rope, CausalLTXAttention, kv_cache, torch)
+    gen_text_cross(CausalLTXAttention, kv_cache, torch)
     gen_cache(kv_cache, tcache, torch, compute_av_blocks)
     gen_a2a()
     import einops

@@ -102,3 +102,22 @@ def test_cat_cache_requires_k_before_v():
     v2 = _cat_cache(v, chunk)
     assert k2._state is v2._state and k2.shape == (1, 12, 2, 8)
     assert k.shape == (1, 8, 2, 8)  # the old view is unchanged
+
+
+def test_key_padding_runs_from_reference_masks():
+    """Key-padding masks in the forms the reference builds become runs of
+    visible keys (host logic; CPU tensors)."""
+    from taomate_b200.attention import key_padding_runs
+    m01 = torch.tensor([[1, 1, 1, 0, 0], [1, 1, 1, 1, 1]])
+    assert key_padding_runs(m01, 2, 5) == [[(0, 3)], [(0, 5)]]
+    # _prepare_attention_mask: (mask - 1) * finfo.max, shape [B, 1, 1, Lk]
+    add = ((m01 - 1).to(torch.bfloat16) * torch.finfo(torch.bfloat16).max).reshape(2, 1, -1, 5)
+    assert key_padding_runs(add, 2, 5) == [[(0, 3)], [(0, 5)]]
+    holes = torch.tensor([[True, False, True, True, False, True]])
+    assert key_padding_runs(holes, 3, 6) == [[(0, 1), (2, 2), (5, 1)]] * 3  # batch broadcast
+    assert key_padding_runs(torch.zeros(1, 4, dtype=torch.bool), 1, 4) == [[]]
+    with pytest.raises(NotImplementedError):
+        key_padding_runs(torch.tensor([[[0.0, -1.5, 0.0]]]), 1, 3)  # a real bias
+    per_query = torch.tensor([[[[1, 0], [0, 1]]]], dtype=torch.bool)
+    with pytest.raises(NotImplementedError):
+        key_padding_runs(per_query, 1, 2)

@@ -310,6 +310,53 @@ def test_attention_with_cache_vs_reference(golden_dir, case):
     assert rel_l2(nv[0], z["new_v_f32"]) < 1.25 * rel_l2(z["new_v_bf16"], z["new_v_f32"])
 
 
+@pytest.mark.parametrize("case", list(inputs.TEXT_CROSS_CASES))
+def test_text_cross_attention_vs_reference(golden_dir, case):
+    """Text cross-attention with cached K/V and the prompt's padding mask
+    (kv_cache.py:764-827) against the reference's fp32 output; the second call
+    is a K/V cache hit and must return the same values."""
+    import taomate_b200 as tm
+    z = np.load(os.path.join(golden_dir, f"text_cross_{case}.npz"))
+    d = inputs.text_cross_inputs(case)
+    c = d["cfg"]
+    attn = make_attn(d)
+    x = _bf(d["x"])
+    ctx = _bf(d["context"])
+    m = torch.from_numpy(d["mask"]).to(DEV)
+    mask = (m - 1).to(torch.bfloat16).reshape(m.shape[0], 1, -1, m.shape[-1]) \
+        * torch.finfo(torch.bfloat16).max
+    with torch.no_grad():
+        out = tm.text_cross_attention_with_kv_cache(attn, x, ctx, mask=mask, base_context=ctx,
+                                                    cache_name="text", layer_idx=0)
+        again = tm.text_cross_attention_with_kv_cache(attn, x, ctx, mask=mask, base_context=ctx,
+                                                      cache_name="text", layer_idx=0)
+    assert len(attn._ltx_text_cross_kv_cache) == 1
+    assert torch.equal(out, again)
+    assert out.shape == (c["batch"], c["lq"], c["hidden"])
+    ref_err = rel_l2(z["out_bf16"], z["out_f32"])
+    assert rel_l2(out, z["out_f32"]) < 1.25 * ref_err
+
+
+def test_standard_attention_forward_key_padding_mask():
+    import taomate_b200 as tm
+    gen = torch.Generator().manual_seed(5)
+    B, Lq, Lk, H, D = 2, 200, 300, 4, 64
+    q = torch.randn(B, Lq, H, D, generator=gen).to(DEV, torch.bfloat16)
+    k = torch.randn(B, Lk, H, D, generator=gen).to(DEV, torch.bfloat16)
+    v = torch.randn(B, Lk, H, D, generator=gen).to(DEV, torch.bfloat16)
+    vis = torch.ones(B, Lk, dtype=torch.bool, device=DEV)
+    vis[0, 250:] = False
+    vis[1, 10:40] = False
+    out = tm.standard_attention_forward(q, k, v, mask=vis)
+    f = lambda t: t.transpose(1, 2).float()
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        f(q), f(k), f(v), attn_mask=vis[:, None, None, :]).transpose(1, 2)
+    refb = torch.nn.functional.scaled_dot_product_attention(
+        f(q).bfloat16(), f(k).bfloat16(), f(v).bfloat16(),
+        attn_mask=vis[:, None, None, :]).transpose(1, 2)
+    assert rel_l2(out, ref) < 1.02 * rel_l2(refb, ref) + 1e-4
+
+
 # ---------------------------------------------------------------- copies and arena
 def test_cat_tensors_bit_exact():
     from taomate_b200.kv_cache import cat_tensors

@@ -95,6 +95,17 @@ def test_attention_with_cache_matches_reference(golden_dir, case):
     assert rel_l2(out, z["out_bf16"]) < 2e-2
 
 
+@pytest.mark.parametrize("case", list(inputs.TEXT_CROSS_CASES))
+def test_text_cross_attention_matches_reference(golden_dir, case):
+    z = _load(golden_dir, f"text_cross_{case}.npz")
+    d = inputs.text_cross_inputs(case)
+    c = d["cfg"]
+    out = O.text_cross_attention(d["x"], d["context"], d["params"], c["heads"], c["dim_head"],
+                                 mask=d["mask"])
+    assert rel_l2(out, z["out_f32"]) < 2e-5
+    assert rel_l2(out, z["out_bf16"]) < 2e-2  # the reference's own bf16 path
+
+
 def test_av_blocks_known_answers(golden_dir):
     with open(os.path.join(golden_dir, "av_blocks.json")) as fh:
         kab = json.load(fh)
