@@ -245,6 +245,10 @@ TM_API int64_t tm_attention_workspace_bytes(int B, int Lq, int H, int D, int64_t
  *                    (out_row_stride >= (head_base + H) * D)
  *   out_delta[i]     bytes from `out` to rank i's output buffer, mapped into
  *                    this process (tm_peer_open); 0 for this rank
+ *   gate_logits      optional [B, Lq, H] bf16 logits (head stride 1, strides in
+ *                    elements): each output row of head h is multiplied by
+ *                    2 * sigmoid(logit) before it is stored — the per-head gate
+ *                    of kv_cache.py:1691-1697 fused into the epilogue
  * Replaces the attention + head->seq all-to-all of attention_with_cache
  * (kv_cache.py:1531-1538, all_to_all.py:154-173).
  */
@@ -255,6 +259,9 @@ typedef struct {
   int32_t rows_per_rank;
   int32_t head_base;
   int64_t out_delta[8];
+  const void* gate_logits;
+  int64_t gate_batch_stride;
+  int64_t gate_row_stride;
 } tm_attention_ext;
 
 TM_API int tm_attention_fwd_ext(const void* q, int64_t q_batch_stride, int64_t q_row_stride,

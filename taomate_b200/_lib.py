@@ -46,7 +46,8 @@ class NormRopeJob(ctypes.Structure):
 class AttentionExt(ctypes.Structure):
     _fields_ = [("device_tiles", c_vp), ("workspace", c_vp), ("workspace_bytes", c_i64),
                 ("rows_per_rank", ctypes.c_int32), ("head_base", ctypes.c_int32),
-                ("out_delta", c_i64 * 8)]
+                ("out_delta", c_i64 * 8), ("gate_logits", c_vp), ("gate_batch_stride", c_i64),
+                ("gate_row_stride", c_i64)]
 
 
 class CopySpan(ctypes.Structure):

@@ -44,7 +44,8 @@ def _row_strides(t: Tensor, H: int, D: int) -> Tuple[int, int]:
 def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tensor],
                     cache_spans: Sequence[Tuple[int, int]], new_k: Optional[Tensor],
                     new_v: Optional[Tensor], new_rows: int, scale: Optional[float] = None,
-                    out: Optional[Tensor] = None, peer=None) -> Tensor:
+                    out: Optional[Tensor] = None, peer=None,
+                    gate_logits: Optional[Tensor] = None) -> Tensor:
     """``softmax(q K^T * scale) V`` with the keys of ``cache_spans`` (row ranges
     of ``cache_k/v``) followed by the first ``new_rows`` rows of ``new_k/v``.
     All tensors ``[B, L, H, D]`` bf16 with contiguous heads.
@@ -52,7 +53,9 @@ def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tens
     With ``peer`` (a :class:`taomate_b200.parallel.PeerExchange`) the kernel
     stores each output row in its owner rank's ``peer.out`` (the fused
     head->seq exchange); the caller then runs ``peer.exchange(1)`` and reads
-    ``peer.out``, which is also what this returns."""
+    ``peer.out``, which is also what this returns.  ``gate_logits``
+    (``[B, Lq, H]`` bf16) multiplies each output row of head h by
+    ``2 * sigmoid(logit)`` in the kernel's epilogue."""
     dev = _lib.require_cuda(q, cache_k, new_k)
     B, Lq, H, D = (int(v) for v in q.shape)
     if q.dtype != torch.bfloat16:
@@ -71,6 +74,12 @@ def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tens
         if out is None:
             out = torch.empty(B, Lq, H, D, device=dev, dtype=torch.bfloat16)
         obs, ors = _row_strides(out, H, D)
+    if gate_logits is not None:
+        if gate_logits.dtype != torch.bfloat16 or gate_logits.shape != (B, Lq, H) or \
+                gate_logits.stride(2) != 1:
+            raise ValueError(f"gate logits must be [B, Lq, H] bf16 with unit head stride")
+        ext.gate_logits = gate_logits.data_ptr()
+        ext.gate_batch_stride, ext.gate_row_stride = gate_logits.stride(0), gate_logits.stride(1)
     spans = [(0, int(s), int(n)) for (s, n) in cache_spans if n > 0]
     if new_k is not None and new_rows > 0:
         spans.append((1, 0, int(new_rows)))
@@ -468,8 +477,12 @@ def attention_with_cache(
     if peer is not None and not (q.data_ptr() >= peer.recv.data_ptr() and
                                  q.data_ptr() < peer.recv.data_ptr() + peer.recv.nbytes):
         peer = None  # this call's exchange went through NCCL
+    # the per-head gate (kv_cache.py:1691-1697) rides in the kernel's epilogue
+    # when the output rows stay on this rank
+    fuse_gate = sp_size == 1 and getattr(attn, "to_gate_logits", None) is not None
+    glog = attn.to_gate_logits(x) if fuse_gate else None
     with section(base + ".sdpa"):
-        out = flash_attention(q, ck, cv, spans, k, v, nk_rows, peer=peer)
+        out = flash_attention(q, ck, cv, spans, k, v, nk_rows, peer=peer, gate_logits=glog)
 
     # 5. head -> seq
     if peer is not None:
@@ -486,7 +499,7 @@ def attention_with_cache(
 
     # 6. gate + out projection (kv_cache.py:1680-1700)
     out = out.reshape(B, -1, H * D)
-    if getattr(attn, "to_gate_logits", None) is not None:
+    if getattr(attn, "to_gate_logits", None) is not None and not fuse_gate:
         gates = 2.0 * torch.sigmoid(attn.to_gate_logits(x))
         out = (out.view(B, -1, H, D) * gates.unsqueeze(-1)).view(B, -1, H * D)
     out = attn.to_out(out)

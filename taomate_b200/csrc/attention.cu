@@ -92,6 +92,10 @@ struct __align__(64) Params {
   int rows_per_rank;
   int head_base;
   int64_t out_delta[8];
+  // Per-head output gate 2 * sigmoid(logit), logits [B, Lq, H] bf16 (head
+  // stride 1), or null.
+  const __nv_bfloat16* gate;
+  int64_t gate_bs, gate_rs;
   float scale_log2;
   int* err;
 };
@@ -143,6 +147,15 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float&
   f2_unpack(pp, p0, p1);
   y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
   y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
+// 2 * sigmoid of the row's gate logit (1 without a gate).
+__device__ __forceinline__ float gate_of(const __nv_bfloat16* gate, int64_t gbs, int64_t grs,
+                                         int batch, int qi, int head) {
+  if (!gate) return 1.0f;
+  const float z = __bfloat162float(gate[static_cast<int64_t>(batch) * gbs +
+                                        static_cast<int64_t>(qi) * grs + head]);
+  return 2.0f / (1.0f + __expf(-z));
 }
 
 // Address of output row qi, head `head`, column 0.
@@ -531,6 +544,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           }
         }
       } else {
+      if (qi < p.Lq) {
+        const float g = gate_of(p.gate, p.gate_bs, p.gate_rs, batch, qi, head);
+        s0 *= g;
+        s1 *= g;
+      }
       __nv_bfloat16* orow = out_row(p.out, p.out_bs, p.out_rs, p.rows_per_rank, p.head_base,
                                     p.out_delta, batch, qi, head, D);
 #pragma unroll
@@ -577,6 +595,8 @@ struct OutPlace {
   int64_t out_bs, out_rs;
   int rows_per_rank, head_base;
   int64_t delta[8];
+  const __nv_bfloat16* gate;
+  int64_t gate_bs, gate_rs;
 };
 
 template <int D>
@@ -615,7 +635,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
       acc[1] += wgt * v.y;
     }
   }
-  const float inv = 1.0f / den;
+  const float inv = gate_of(op.gate, op.gate_bs, op.gate_rs, b, qi, h) / den;
   __nv_bfloat16* dst = out_row(op.out, op.out_bs, op.out_rs, op.rows_per_rank, op.head_base,
                                op.delta, b, qi, h, D) + lane * kPer;
   if constexpr (kPer == 4) {
@@ -678,6 +698,9 @@ static int launch(Params& prm, int B, int Lq, int H, cudaStream_t stream) {
   op.rows_per_rank = prm.rows_per_rank;
   op.head_base = prm.head_base;
   for (int i = 0; i < 8; ++i) op.delta[i] = prm.out_delta[i];
+  op.gate = prm.gate;
+  op.gate_bs = prm.gate_bs;
+  op.gate_rs = prm.gate_rs;
   combine_kernel<D><<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(
       prm.part_o, prm.part_ml, prm.kv_splits, B, Lq, H, op);
   return check_cuda(cudaGetLastError(), "attention: combine launch");
@@ -865,6 +888,14 @@ static int attention_impl(const void* q, int64_t q_batch_stride, int64_t q_row_s
     if (ext.out_delta[i] & 15)
       return set_error(TM_ERR_ALIGNMENT, "attention: output offset %d not 16-byte aligned", i);
     prm.out_delta[i] = ext.out_delta[i];
+  }
+  if (ext.gate_logits) {
+    if (ext.gate_row_stride < H || ext.gate_batch_stride < 0)
+      return set_error(TM_ERR_INVALID_ARGUMENT, "attention: gate row stride %lld < H",
+                       (long long)ext.gate_row_stride);
+    prm.gate = static_cast<const __nv_bfloat16*>(ext.gate_logits);
+    prm.gate_bs = (B == 1) ? 0 : ext.gate_batch_stride;
+    prm.gate_rs = ext.gate_row_stride;
   }
   const double sc = (scale > 0.f) ? (double)scale : 1.0 / std::sqrt((double)D);
   prm.scale_log2 = static_cast<float>(sc * 1.4426950408889634);

@@ -493,3 +493,23 @@ def test_attention_key_range_split_and_plain_entry_agree():
     assert_attention_parity(out_ws, q, [k], [v])
     assert_attention_parity(out_plain, q, [k], [v])
     assert rel_l2(out_ws, out_plain) < 4e-3
+
+
+@pytest.mark.parametrize("H", [32, 4])
+def test_attention_fused_gate(H):
+    """The per-head gate 2*sigmoid(logit) applied in the epilogue (pair CTAs at
+    32 heads) and in the key-range merge (4 heads) against gating the fp32
+    reference afterwards."""
+    from taomate_b200 import flash_attention
+    gen = torch.Generator().manual_seed(21 + H)
+    D, Lq, Lk = 128, 1152, 2304
+    q = torch.randn(1, Lq, H, D, generator=gen).to(DEV, torch.bfloat16)
+    k = torch.randn(1, Lk, H, D, generator=gen).to(DEV, torch.bfloat16)
+    v = torch.randn(1, Lk, H, D, generator=gen).to(DEV, torch.bfloat16)
+    logits = (torch.randn(1, Lq, H, generator=gen) * 2).to(DEV, torch.bfloat16)
+    out = flash_attention(q, None, None, [], k, v, Lk, gate_logits=logits)
+    g = (2.0 * torch.sigmoid(logits.float()))[..., None]
+    ref = _sdpa_ref(q, [k], [v]) * g
+    refb = _sdpa_bf16(q, [k], [v]).float() * g
+    assert torch.isfinite(out).all()
+    assert rel_l2(out, ref) < 1.02 * rel_l2(refb, ref) + 1e-4
