@@ -152,3 +152,80 @@ def retain_window(cache: KVCache, anchor_tokens: int, window_tokens: int,
             kw[name + "_k"], kw[name + "_v"] = _slice_pair(k, v, spans)
         layers.append(LayerKVCache(**kw))
     return KVCache(layers=layers)
+
+
+# ---------------------------------------------------------------------------
+# Conditioning refresh (taomate/inference/runtime.py:386-470,
+# taomate/inference/streaming_runtime.py:1003-1200)
+# ---------------------------------------------------------------------------
+AUDIO_FRAMES_PER_BLOCK = 25    # ltx_causal/attention/mask_builder.py:97
+AUDIO_FRAMES_FIRST_BLOCK = 26  # mask_builder.py:99
+
+
+def compute_av_blocks(total_video_latent_frames: int, num_frame_per_block: int = 3,
+                      num_frame_per_block_first: int = 0) -> List[Tuple[int, int, int, int, int]]:
+    """``(block_idx, video_start, video_end, audio_start, audio_end)`` of the
+    streaming blocks (mask_builder.py:102-186): an optional longer first block
+    (26 audio frames), then blocks of ``num_frame_per_block`` video frames with
+    25 audio frames each (a short last block gets the proportional share)."""
+    if num_frame_per_block_first > 0:
+        if total_video_latent_frames < num_frame_per_block_first:
+            raise AssertionError(f"{total_video_latent_frames} frames < first block "
+                                 f"{num_frame_per_block_first}")
+        out = [(0, 0, num_frame_per_block_first, 0, AUDIO_FRAMES_FIRST_BLOCK)]
+    else:
+        if total_video_latent_frames < 1:
+            raise AssertionError("need at least one video frame")
+        out = [(0, 0, 1, 0, 1)]
+    b, v, a = 1, out[0][2], out[0][4]
+    while v < total_video_latent_frames:
+        ve = min(v + num_frame_per_block, total_video_latent_frames)
+        n = ve - v
+        ae = a + (AUDIO_FRAMES_PER_BLOCK if n == num_frame_per_block
+                  else AUDIO_FRAMES_PER_BLOCK * n // num_frame_per_block)
+        out.append((b, v, ve, a, ae))
+        b, v, a = b + 1, ve, ae
+    return out
+
+
+def refresh_blocks(segments: List[Dict[str, int]], prefix_frames: int, next_frames: int,
+                   num_frame_per_block: int = 3, num_frame_per_block_first: int = 4):
+    """The retained prefix blocks whose K/V a prompt change re-prefills, one
+    per retained segment in order (streaming_runtime.py:1037-1075,
+    runtime.py:398-419): the local sink block when the cache keeps the sink,
+    then the newest warm blocks of the retained latent prefix."""
+    if not segments:
+        raise RuntimeError("Selective KV rebuild requires committed segment metadata")
+    blocks = compute_av_blocks(prefix_frames + next_frames, num_frame_per_block,
+                               num_frame_per_block_first)
+    prefix = [blk for blk in blocks if blk[2] <= prefix_frames]
+    if not prefix:
+        raise RuntimeError("Selective KV rebuild received an empty latent prefix")
+    has_sink = int(segments[0].get("block_idx", -1)) == 0
+    warm = len(segments) - (1 if has_sink else 0)
+    candidates = prefix[1:] if has_sink else prefix
+    if warm > len(candidates):
+        raise ValueError(f"Selective KV rebuild does not have enough retained prefix latents: "
+                         f"segments={len(segments)}, warm_needed={warm}, "
+                         f"warm_available={len(candidates)}")
+    picked = ([prefix[0]] if has_sink else []) + (candidates[-warm:] if warm > 0 else [])
+    if len(picked) != len(segments):
+        raise RuntimeError("Selective KV latent/segment layout mismatch")
+    return picked
+
+
+def replace_modal_fields(cache: KVCache, rebuilt: KVCache,
+                         keep: Tuple[str, ...] = ("video_self",)) -> KVCache:
+    """Every cache field except ``keep`` taken from ``rebuilt`` (the
+    re-prefilled prompt-sensitive K/V), video self-attention K/V kept
+    (runtime.py:458-466): a field swap per layer, no data moves; the segment
+    metadata stays attached."""
+    if rebuilt is None or len(rebuilt.layers) != len(cache.layers):
+        raise RuntimeError("Conditioning cache refresh failed.")
+    segments = cache_segments(cache)
+    kept = {f + s for f in keep for s in ("_k", "_v")}
+    for layer, new in zip(cache.layers, rebuilt.layers):
+        for f in LayerKVCache.__dataclass_fields__:
+            if f not in kept:
+                setattr(layer, f, getattr(new, f))
+    return attach_segments(cache, segments)

@@ -121,3 +121,49 @@ def test_key_padding_runs_from_reference_masks():
     per_query = torch.tensor([[[[1, 0], [0, 1]]]], dtype=torch.bool)
     with pytest.raises(NotImplementedError):
         key_padding_runs(per_query, 1, 2)
+
+
+def test_compute_av_blocks_matches_oracle():
+    from oracle import ltx_oracle as O
+    for total in (4, 5, 7, 16, 18, 31):
+        for first in (0, 4):
+            if first and total < first:
+                continue
+            assert C.compute_av_blocks(total, 3, first) == [tuple(b) for b in
+                                                           O.compute_av_blocks(total, 3, first)]
+
+
+def test_refresh_blocks_select_sink_and_newest_warm_blocks():
+    # retained: sink block 0 plus the two newest warm blocks, prefix of 16 frames
+    segs = [{"block_idx": 0, "video_tokens": 4, "audio_tokens": 26},
+            {"block_idx": 7, "video_tokens": 3, "audio_tokens": 25},
+            {"block_idx": 8, "video_tokens": 3, "audio_tokens": 25}]
+    picked = C.refresh_blocks(segs, prefix_frames=16, next_frames=3)
+    blocks = C.compute_av_blocks(19, 3, 4)
+    prefix = [b for b in blocks if b[2] <= 16]
+    assert picked == [prefix[0], prefix[-2], prefix[-1]]
+    # no sink retained: the newest blocks only
+    assert C.refresh_blocks(segs[1:], 16, 3) == prefix[-2:]
+    with pytest.raises(ValueError, match="not have enough"):
+        C.refresh_blocks(segs + [dict(block_idx=9, video_tokens=3, audio_tokens=25)] * 9, 7, 3)
+    with pytest.raises(RuntimeError):
+        C.refresh_blocks([], 16, 3)
+
+
+def test_replace_modal_fields_keeps_video_self():
+    segs = [{"block_idx": 0, "video_tokens": 8, "audio_tokens": 0}]
+    a = _arena()
+    vk, vv = _pair_with(a, [8])
+    old = LayerKVCache(video_self_k=vk, video_self_v=vv, audio_self_k=torch.zeros(1),
+                       audio_self_v=torch.zeros(1))
+    new = LayerKVCache(video_self_k=torch.ones(2), video_self_v=torch.ones(2),
+                       audio_self_k=torch.ones(3), audio_self_v=torch.ones(3),
+                       a2v_k=torch.ones(4), a2v_v=torch.ones(4))
+    cache = C.attach_segments(KVCache(layers=[old]), segs)
+    out = C.replace_modal_fields(cache, KVCache(layers=[new]))
+    lay = out.layers[0]
+    assert lay.video_self_k is vk and lay.video_self_v is vv
+    assert lay.audio_self_k is new.audio_self_k and lay.a2v_v is new.a2v_v
+    assert C.cache_segments(out) == segs
+    with pytest.raises(RuntimeError):
+        C.replace_modal_fields(cache, KVCache(layers=[]))
