@@ -301,7 +301,8 @@ def run_ours(args):
         number of key tiles; per block only the tile table, the RoPE tables and
         the inputs change."""
 
-        def __init__(self, cache, block):
+        def __init__(self, cache, block, inputs):
+            self.inputs = inputs  # the per-layer inputs the captured forward reads
             c, s = tables(block)
             self.pe = (c.contiguous(), s.contiguous())
             for lay in cache.layers:  # pending chunks go to their slots before capture
@@ -312,8 +313,9 @@ def run_ours(args):
                 kv, out = [], None
                 for li in range(L):
                     lay = cache.layers[li]
-                    out, nk, nv = tm.attention_with_cache(attn[li], xs[li], None, self.pe, None,
-                                                          lay.video_self_k, lay.video_self_v)
+                    out, nk, nv = tm.attention_with_cache(attn[li], inputs[li], None, self.pe,
+                                                          None, lay.video_self_k,
+                                                          lay.video_self_v)
                     kv.append((nk, nv))
                 return out, kv
 
@@ -346,13 +348,18 @@ def run_ours(args):
             outs = [torch.empty(1, S_loc, HIDDEN, dtype=torch.bfloat16).pin_memory()
                     for _ in range(FORWARDS_PER_STEP)]
         block = 0
-        runner = None
+        runners = []
         with torch.no_grad():
             for _ in range(n_warm):
                 cache = step(cache, block)
                 block += 1
             if graphed:
-                runner = GraphRunner(cache, block)
+                runners.append(GraphRunner(cache, block, xs))
+                if host_io:
+                    # a second captured forward with its own inputs: the next step's
+                    # host-to-device copy overlaps this step's forwards
+                    runners.append(GraphRunner(cache, block, [torch.empty_like(x) for x in xs]))
+        runner = runners[0] if runners else None
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -365,11 +372,32 @@ def run_ours(args):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         with torch.no_grad():
-            for _ in range(n_steps):
-                if runner is not None:
-                    if host_io:  # the captured forward reads xs
+            if runner is not None and host_io:
+                main = torch.cuda.current_stream(dev)
+                cs = torch.cuda.Stream(dev)
+                ready = [torch.cuda.Event(), torch.cuda.Event()]
+                done = [None, None]
+
+                def upload(r):
+                    with torch.cuda.stream(cs):
+                        if done[r] is not None:
+                            cs.wait_event(done[r])  # its previous forwards have read it
                         for li in range(L):
-                            xs[li].copy_(x_host[li], non_blocking=True)
+                            runners[r].inputs[li].copy_(x_host[li], non_blocking=True)
+                        ready[r].record(cs)
+
+                cs.wait_stream(main)
+                upload(0)
+            for i in range(n_steps):
+                if runner is not None and host_io:
+                    r = i % 2
+                    main.wait_event(ready[r])
+                    if i + 1 < n_steps:
+                        upload(1 - r)
+                    cache = runners[r].step(cache, block, outs)
+                    done[r] = torch.cuda.Event()
+                    done[r].record(main)
+                elif runner is not None:
                     cache = runner.step(cache, block, outs)
                 elif host_io:
                     for li in range(L):
@@ -391,9 +419,10 @@ def run_ours(args):
             dist.barrier()
         h2d = sum(x.numel() * x.element_size() for x in xs) if host_io else 0
         d2h = FORWARDS_PER_STEP * S_loc * HIDDEN * 2 if host_io else 0
-        if runner is not None:
-            runner.graph.reset()  # before the process group its exchanges use goes away
-            del runner
+        for r in runners:
+            r.graph.reset()  # before the process group its exchanges use goes away
+        runners.clear()
+        runner = None
         return ms, launches, clocks, h2d, d2h
 
     graphed = not args.eager
