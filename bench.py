@@ -227,7 +227,7 @@ def run_ours(args):
     from taomate_b200 import _lib, parallel as P
     from taomate_b200.attention import AttentionWeights
     from taomate_b200.cache import retain_window
-    from taomate_b200.graphs import AttentionGraph, attention_spans
+    from taomate_b200.graphs import AttentionGraph, attention_spans, copy_into
     from taomate_b200.kv_cache import ArenaSpec, KVCache, LayerKVCache, init_arena_cache
     from taomate_b200.profiler import TIMER
 
@@ -323,8 +323,8 @@ def run_ours(args):
 
         def step(self, cache, block, outs=None):
             c, s = tables(block)  # once per block: the four forwards share the start frame
-            self.pe[0].copy_(c)
-            self.pe[1].copy_(s)
+            copy_into(self.pe[0], c)  # kernel copies: nothing queues behind the input upload
+            copy_into(self.pe[1], s)
             spans = [attention_spans(lay.video_self_k, lay.video_self_v, Lq)
                      for lay in cache.layers]
             for fwd in range(FORWARDS_PER_STEP):

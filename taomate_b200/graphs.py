@@ -10,8 +10,8 @@ included) and replays it.
 What changes between the streaming blocks is where the cache rows sit in the
 slot arena: every attention call of a captured forward therefore reads its key
 tiles from one device table instead of its launch parameters, and
-``replay(site_spans)`` rewrites that table from the new cache layout with one
-host-to-device copy before the replay.  A block may replay the graph as long
+``replay(site_spans)`` rewrites that table from the new cache layout before the
+replay (a small kernel reads the pinned staging buffer).  A block may replay the graph as long
 as every attention call keeps the tile count it was captured with (the window
 is full); anything else must recapture.  Inputs and outputs of a replay are the
 tensors the captured forward read and returned (the graph's own memory).
@@ -144,8 +144,12 @@ class AttentionGraph:
             self._dirty = True
         if self._dirty:
             with torch.cuda.stream(stream):
-                self.table[:self._used].copy_(self._stage[self._cur][:self._used],
-                                              non_blocking=True)
+                # A kernel reads the pinned staging buffer (mapped into the GPU's
+                # address space): a copy-engine transfer here would queue behind
+                # bulk host transfers of other streams and stall the replay.
+                nbytes = (self._used * 4 + 15) // 16 * 16
+                copy_bytes(self.table.data_ptr(), self._stage[self._cur].data_ptr(), nbytes,
+                           self.device)
                 ev = torch.cuda.Event()
                 ev.record(stream)
             self._events[self._cur] = ev
@@ -158,6 +162,35 @@ class AttentionGraph:
         use is destroyed)."""
         self.graph = None
         self.sites = []
+
+
+def copy_bytes(dst: int, src: int, nbytes: int, device: torch.device) -> None:
+    """Copy ``nbytes`` (a multiple of 16) with the row-copy kernel on the
+    current stream; ``src`` may be pinned host memory."""
+    span = (_lib.CopySpan * 1)()
+    span[0].src, span[0].dst, span[0].rows = src, dst, 1
+    span[0].src_row_stride = span[0].dst_row_stride = nbytes
+    _lib.check(_lib.load().tm_copy_rows(span, 1, nbytes, _lib.stream_ptr(device)), "copy_bytes")
+    _lib.launched()
+
+
+def copy_into(dst: torch.Tensor, src: torch.Tensor) -> None:
+    """``dst.copy_(src)`` for ``[1, H, R, W]`` tensors with contiguous rows,
+    with the row-copy kernel (no copy engine; see ``AttentionGraph.replay``)."""
+    if dst.shape != src.shape or dst.dtype != src.dtype or dst.dim() != 4 or dst.shape[0] != 1 \
+            or dst.stride(3) != 1 or src.stride(3) != 1:
+        raise ValueError("copy_into takes equal [1, H, R, W] tensors with unit column stride")
+    H, R = int(dst.shape[1]), int(dst.shape[2])
+    row = int(dst.shape[3]) * dst.element_size()
+    if H > 64 or row % 16:
+        raise ValueError("copy_into: at most 64 heads, rows a multiple of 16 bytes")
+    spans = (_lib.CopySpan * H)()
+    for h in range(H):
+        spans[h].src, spans[h].dst, spans[h].rows = src[0, h].data_ptr(), dst[0, h].data_ptr(), R
+        spans[h].src_row_stride = src.stride(2) * src.element_size()
+        spans[h].dst_row_stride = dst.stride(2) * dst.element_size()
+    _lib.check(_lib.load().tm_copy_rows(spans, H, row, _lib.stream_ptr(dst.device)), "copy_into")
+    _lib.launched()
 
 
 def attention_spans(cached_k, cached_v, new_rows: int) -> List[Tuple[int, int, int]]:
