@@ -63,7 +63,7 @@ def parse():
     ap.add_argument("--eager", action="store_true",
                     help="issue every forward from Python instead of replaying a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-case", choices=["attention", "norm_rope"], default=None,
+    ap.add_argument("--kernel-case", choices=["attention", "norm_rope", "kv_append"], default=None,
                     help="time one kernel in isolation at C2 shapes (profiling target)")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--heads", type=int, default=None,
@@ -516,6 +516,18 @@ def run_kernel_case(args):
         out = torch.empty_like(q)
         fn = lambda: tm.flash_attention(q, ck, cv, [(0, Lc)], nk, nv, Lq, out=out)
         work, unit = 4.0 * Lq * (Lc + Lq) * Hk * DIM_HEAD / 1e12, "TFLOP/s"
+    elif args.kernel_case == "kv_append":
+        # the commit append: one block's K and V [1152, 32, 128] into an arena slot
+        from taomate_b200.kv_cache import KVArena
+        arena = KVArena(2, Lq, 1, HEADS, DIM_HEAD, dtype=torch.bfloat16, device=dev)
+        nk, nv = rnd(1, Lq, HEADS, DIM_HEAD), rnd(1, Lq, HEADS, DIM_HEAD)
+
+        def fn():
+            ents = arena.write(nk, nv)
+            for (slot, _, _) in ents:  # give the slot back: the same copy every launch
+                arena._ref(slot, -1)
+
+        work, unit = 4.0 * Lq * HEADS * DIM_HEAD * 2 / 1e9, "GB/s"
     else:
         xq, xk = rnd(1, Lq, HIDDEN), rnd(1, Lq, HIDDEN)
         w = torch.ones(HIDDEN, device=dev, dtype=torch.bfloat16)
