@@ -62,6 +62,8 @@ def parse():
                          "the kernels' NVLink peer stores")
     ap.add_argument("--eager", action="store_true",
                     help="issue every forward from Python instead of replaying a CUDA graph")
+    ap.add_argument("--qkv3", action="store_true",
+                    help="three projection GEMMs per call instead of one over the fused weights")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-case", choices=["attention", "norm_rope", "kv_append"], default=None,
                     help="time one kernel in isolation at C2 shapes (profiling target)")
@@ -252,6 +254,9 @@ def run_ours(args):
 
     torch.manual_seed(0)  # identical weights on every rank
     attn = [AttentionWeights(HIDDEN, HEADS, DIM_HEAD, device=dev) for _ in range(L)]
+    if not args.qkv3:
+        for a in attn:  # one projection GEMM per call (weights laid out as one buffer)
+            tm.fuse_qkv_weights(a)
     gen = torch.Generator(device=dev).manual_seed(1)
     xs = [torch.randn(1, Lq, HIDDEN, device=dev, generator=gen).to(torch.bfloat16)
           [:, rank * S_loc:(rank + 1) * S_loc].contiguous() for _ in range(L)]
@@ -315,7 +320,8 @@ def run_ours(args):
                     lay = cache.layers[li]
                     out, nk, nv = tm.attention_with_cache(attn[li], inputs[li], None, self.pe,
                                                           None, lay.video_self_k,
-                                                          lay.video_self_v)
+                                                          lay.video_self_v,
+                                                          profile_name="video_self")
                     kv.append((nk, nv))
                 return out, kv
 
@@ -339,7 +345,7 @@ def run_ours(args):
                 new_layers.append(LayerKVCache(video_self_k=k2, video_self_v=v2))
             return retain_window(KVCache(layers=new_layers), anchor, window)
 
-    def timed(n_steps, n_warm, host_io, graphed=False):
+    def timed(n_steps, n_warm, host_io, graphed=False, sections=False):
         cache = fresh_cache()
         x_host = outs = None
         if host_io:
@@ -354,7 +360,10 @@ def run_ours(args):
                 cache = step(cache, block)
                 block += 1
             if graphed:
+                if sections:
+                    TIMER.start()  # the sections become event nodes of the captured graph
                 runners.append(GraphRunner(cache, block, xs))
+                TIMER.stop()
                 if host_io:
                     # a second captured forward with its own inputs: the next step's
                     # host-to-device copy overlaps this step's forwards
@@ -365,7 +374,7 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
         l0 = _lib.LAUNCHES
-        if not host_io:
+        if sections and not graphed:
             TIMER.start()
         sampler = ClockSampler(local)
         sampler.start()
@@ -428,10 +437,10 @@ def run_ours(args):
     graphed = not args.eager
     ms, launches, clocks, _, _ = timed(args.steps, args.warmup, host_io=False, graphed=graphed)
     value = Q_FRAMES * args.steps / (ms / 1e3)
-    if graphed:
-        # A replayed graph cannot bracket single kernels with events: the
-        # attention launches are timed in an eager pass of the same steps.
-        timed(args.steps, args.warmup, host_io=False, graphed=False)
+    # Per-section times (the attention launch among them) come from a second
+    # pass of the same steps whose captured forward also holds event nodes
+    # around each section; the headline pass above has none.
+    timed(args.steps, args.warmup, host_io=False, graphed=graphed, sections=True)
     sections = TIMER.summary()
 
     e2e = None
@@ -482,6 +491,7 @@ def run_ours(args):
                                        + ("nccl all_to_all" if args.nccl_exchange
                                           else "fused NVLink peer stores"))
                                       if sp > 1 else "single gpu",
+                       "projections": "three GEMMs" if args.qkv3 else "one fused QKV GEMM",
                        "executor": "cuda graph per forward (eager warm-up, capture at the full "
                                    "window)" if graphed else "eager",
                        "l2": "inputs larger than L2 (48 layers of weights, caches and "

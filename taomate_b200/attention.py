@@ -5,7 +5,8 @@
 that of ``ltx_causal/attention/flex_attention_utils.py:225-276``.
 
 Per call (video self-attention, C2 shapes):
-  1. projections ``to_q/to_k/to_v`` (cuBLAS GEMMs through torch);
+  1. projections ``to_q/to_k/to_v`` (cuBLAS GEMMs through torch; one GEMM
+     for a module prepared by ``fuse_qkv_weights``);
   2. ONE fused kernel: q/k RMSNorm over the inner dim + split RoPE (+ the V
      layout copy), storing straight into the Ulysses send buffer when SP is on;
   3. under SP, ONE NCCL all-to-all for Q, K and V together;
@@ -334,47 +335,89 @@ def _cache_source(cached_k, cached_v):
     return cached_k, cached_v, [(0, int(cached_k.shape[1]))]
 
 
-_SIDE_STREAMS = {}
+def fuse_qkv_weights(attn) -> bool:
+    """Lay ``to_q``, ``to_k`` and ``to_v`` of a self-attention module out as one
+    ``[3 * inner, in]`` weight buffer (and one bias buffer): the three
+    parameters become row blocks of it, with their values unchanged, so
+    ``attention_with_cache`` runs the three projections of a self-attention
+    call as ONE GEMM.  At the short chunks of a streaming step (1152 rows, or
+    1152 / G per GPU under sequence parallelism) one GEMM with three times the
+    columns fills the SMs better than three.  Returns False (and changes
+    nothing) when the three linears differ in shape, dtype, device or bias.
+
+    Reference counterpart: none (the reference runs the three linears,
+    ltx_causal/transformer/kv_cache.py:1380-1410); a loader calls this once
+    per module after loading weights.  Weights later loaded in place
+    (``load_state_dict``, ``copy_``) land in the shared buffer; a parameter
+    that is replaced by a new tensor ends the fusion for that module.
+    """
+    lins = (attn.to_q, attn.to_k, attn.to_v)
+    ws = [l.weight for l in lins]
+    bs = [l.bias for l in lins]
+    w0 = ws[0]
+    if any(w.shape != w0.shape or w.dtype != w0.dtype or w.device != w0.device for w in ws):
+        return False
+    if any((b is None) != (bs[0] is None) for b in bs):
+        return False
+    if bs[0] is not None and any(b.shape != bs[0].shape or b.dtype != bs[0].dtype for b in bs):
+        return False
+    n = int(w0.shape[0])
+    with torch.no_grad():
+        W = torch.cat([w.detach() for w in ws]).contiguous()
+        Bv = torch.cat([b.detach() for b in bs]).contiguous() if bs[0] is not None else None
+        for i, l in enumerate(lins):
+            l.weight.data = W[i * n:(i + 1) * n]
+            if Bv is not None:
+                l.bias.data = Bv[i * n:(i + 1) * n]
+    attn._tm_qkv = (W, Bv)
+    return True
 
 
-def _linear_into(out2d: Tensor, x: Tensor, lin) -> None:
-    x2d = x.reshape(-1, x.shape[-1])
-    if lin.bias is not None:
-        torch.addmm(lin.bias, x2d, lin.weight.t(), out=out2d)
-    else:
-        torch.mm(x2d, lin.weight.t(), out=out2d)
+def _fused_qkv(attn):
+    """The fused QKV buffers of ``fuse_qkv_weights`` while the module's three
+    parameters still point into them, else None."""
+    f = getattr(attn, "_tm_qkv", None)
+    if f is None:
+        return None
+    W, Bv = f
+    n = W.shape[0] // 3
+    for i, l in enumerate((attn.to_q, attn.to_k, attn.to_v)):
+        if l.weight.data_ptr() != W[i * n].data_ptr() or l.weight.shape[0] != n:
+            return None
+        if Bv is not None and (l.bias is None or l.bias.data_ptr() != Bv[i * n:].data_ptr()):
+            return None
+    return f
 
 
 def _projections(attn, x: Tensor, ctx: Tensor):
-    """q, k, v projections.  While a CUDA graph is being captured and the
-    chunk is short (a sequence-parallel shard), k and v run on two side
-    streams next to q: one 144-row GEMM fills a fraction of the SMs, three
-    side by side fill more, at no cost when the graph replays."""
-    if not (x.is_cuda and x.shape[1] <= 576 and torch.cuda.is_current_stream_capturing()):
-        return (F.linear(x, attn.to_q.weight, attn.to_q.bias),
-                F.linear(ctx, attn.to_k.weight, attn.to_k.bias),
-                F.linear(ctx, attn.to_v.weight, attn.to_v.bias))
-    dev = x.device
-    side = _SIDE_STREAMS.get(dev.index)
-    if side is None:
-        side = _SIDE_STREAMS[dev.index] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
-    main = torch.cuda.current_stream(dev)
-    B = x.shape[0]
-    # outputs allocated on the main stream, which joins the side streams
-    # before anything reads or frees them
-    q = torch.empty(B, x.shape[1], attn.to_q.weight.shape[0], device=dev, dtype=x.dtype)
-    k = torch.empty(B, ctx.shape[1], attn.to_k.weight.shape[0], device=dev, dtype=x.dtype)
-    v = torch.empty(B, ctx.shape[1], attn.to_v.weight.shape[0], device=dev, dtype=x.dtype)
-    for st in side:
-        st.wait_stream(main)
-    with torch.cuda.stream(side[0]):
-        _linear_into(k.view(-1, k.shape[-1]), ctx, attn.to_k)
-    with torch.cuda.stream(side[1]):
-        _linear_into(v.view(-1, v.shape[-1]), ctx, attn.to_v)
-    _linear_into(q.view(-1, q.shape[-1]), x, attn.to_q)
-    for st in side:
-        main.wait_stream(st)
-    return q, k, v
+    """q, k, v projections (cuBLAS through torch).  For self-attention over a
+    module prepared by ``fuse_qkv_weights`` one GEMM computes all three, and
+    q, k, v are column slices of its ``[B, L, 3 * inner]`` output."""
+    f = _fused_qkv(attn) if ctx is x else None
+    if f is not None:
+        qkv = F.linear(x, f[0], f[1])
+        return qkv.split(f[0].shape[0] // 3, dim=-1)
+    return (F.linear(x, attn.to_q.weight, attn.to_q.bias),
+            F.linear(ctx, attn.to_k.weight, attn.to_k.bias),
+            F.linear(ctx, attn.to_v.weight, attn.to_v.bias))
+
+
+def _copy_kv(k: Tensor, v: Tensor) -> Tuple[Tensor, Tensor]:
+    """Contiguous copies of two ``[1, L, H, D]`` row-strided views in one
+    launch of the row-copy kernel."""
+    dev = k.device
+    outs = (torch.empty(k.shape, dtype=k.dtype, device=dev),
+            torch.empty(v.shape, dtype=v.dtype, device=dev))
+    row = int(k.shape[2]) * int(k.shape[3]) * k.element_size()
+    spans = (_lib.CopySpan * 2)()
+    for i, (src, dst) in enumerate(((k, outs[0]), (v, outs[1]))):
+        spans[i].src, spans[i].dst, spans[i].rows = src.data_ptr(), dst.data_ptr(), int(src.shape[1])
+        spans[i].src_row_stride = src.stride(1) * src.element_size()
+        spans[i].dst_row_stride = row
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().tm_copy_rows(spans, 2, row, _lib.stream_ptr(dev)), "new K/V copy")
+        _lib.launched()
+    return outs
 
 
 def attention_with_cache(
@@ -411,20 +454,24 @@ def attention_with_cache(
     if sp_size > 1 and not sp_context_sharded:
         raise NotImplementedError("text cross-attention (replicated K/V) is not on this path")
 
+    base = profile_name or ("self" if context is None else "cross")
     # 1. projections (library GEMMs)
-    q, k, v = _projections(attn, x, ctx)
+    with section(base + ".qkv_proj_norm"):
+        q, k, v = _projections(attn, x, ctx)
     q_pe = pe
     kk_pe = k_pe if k_pe is not None else pe
     eps_q, eps_k = _norm_eps(attn.q_norm), _norm_eps(attn.k_norm)
     if abs(eps_q - eps_k) > 0:
         raise NotImplementedError("q_norm and k_norm with different eps")
 
-    base = profile_name or ("self" if context is None else "cross")
     # 2-3. fused norm + RoPE (+ send layout) and the seq->head exchange
     if sp_size == 1:
+        # fused QKV: q and k are normalised in place, so the new K and V the
+        # kernel reads (and this call returns) share one row stride
+        inplace = not v.is_contiguous() and k.stride() == v.stride()
         with section(base + ".rope_reshape"):
             q, k = norm_rope([q, k], [attn.q_norm.weight, attn.k_norm.weight], [q_pe, kk_pe], H,
-                             D, eps_q)
+                             D, eps_q, inplace=inplace)
         v = v.view(B, -1, H, D)
         if logit_log_scale is not None:
             s = logit_log_scale.to(q.dtype)
@@ -489,7 +536,8 @@ def attention_with_cache(
         # The returned cache K/V must outlive the receive buffer: copy them
         # before signalling, since after it the peers may store the next
         # call's rows there.
-        k, v = k.contiguous(), v.contiguous()
+        with section(base + ".new_kv_copy"):
+            k, v = _copy_kv(k, v)
         with section(base + ".a2a_head2seq"):
             peer.exchange(1)
         out = peer.out
@@ -498,11 +546,12 @@ def attention_with_cache(
             out = P.head_all_to_all_seq(out, P.get_sp_group(), sp_size)
 
     # 6. gate + out projection (kv_cache.py:1680-1700)
-    out = out.reshape(B, -1, H * D)
-    if getattr(attn, "to_gate_logits", None) is not None and not fuse_gate:
-        gates = 2.0 * torch.sigmoid(attn.to_gate_logits(x))
-        out = (out.view(B, -1, H, D) * gates.unsqueeze(-1)).view(B, -1, H * D)
-    out = attn.to_out(out)
+    with section(base + ".out_proj"):
+        out = out.reshape(B, -1, H * D)
+        if getattr(attn, "to_gate_logits", None) is not None and not fuse_gate:
+            gates = 2.0 * torch.sigmoid(attn.to_gate_logits(x))
+            out = (out.view(B, -1, H, D) * gates.unsqueeze(-1)).view(B, -1, H * D)
+        out = attn.to_out(out)
     return out, k, v
 
 

@@ -5,8 +5,14 @@ The counterpart of the reference's ``_BlockProfiler``
 events on the current stream with no host synchronisation; ``summary()``
 synchronises once and aggregates milliseconds per section name.  Section
 names follow the reference's (``<profile_base>.rope_reshape``, ``.sdpa``,
-``.a2a_seq2head``, ``.a2a_head2seq``, ``.cache_append``).  Disabled (the
-default) it costs one attribute check per section.
+``.a2a_seq2head``, ``.a2a_head2seq``, ``.cache_append``, ``.qkv_proj_norm``,
+``.out_proj``; here ``qkv_proj_norm`` covers the projection GEMMs only, the
+q/k norms being fused into ``rope_reshape``).  Disabled (the default) it costs
+one attribute check per section.
+
+A section opened while a CUDA graph is being captured records *external*
+events, which become event-record nodes of the graph: every replay then
+re-records them, and ``summary()`` reports the sections of the latest replay.
 """
 
 from __future__ import annotations
@@ -35,8 +41,9 @@ class SectionTimer:
         if not self.enabled:
             yield
             return
-        s = torch.cuda.Event(enable_timing=True)
-        e = torch.cuda.Event(enable_timing=True)
+        ext = torch.cuda.is_current_stream_capturing()
+        s = torch.cuda.Event(enable_timing=True, external=ext)
+        e = torch.cuda.Event(enable_timing=True, external=ext)
         s.record()
         try:
             yield

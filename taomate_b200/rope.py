@@ -131,7 +131,7 @@ def _pe_strides(cos: torch.Tensor) -> Tuple[int, int, int]:
 
 
 def norm_rope(xs, weights, pes, heads: int, dim_head: int, eps: float, sp_size: int = 1,
-              packed: bool = False, peer=None):
+              packed: bool = False, peer=None, inplace: bool = False):
     """Fused RMSNorm + split RoPE over up to four ``[B, L, H*D]`` bf16 tensors
     in one launch (weight ``None`` skips the norm, pe ``None`` skips the
     rotation, both ``None`` is a layout copy).
@@ -144,6 +144,12 @@ def norm_rope(xs, weights, pes, heads: int, dim_head: int, eps: float, sp_size: 
     :class:`taomate_b200.parallel.PeerExchange`, packed jobs only) the kernel
     stores head group g straight into rank g's receive buffer, at this rank's
     slot; the caller then runs ``peer.exchange(0)`` and reads ``peer.recv``.
+
+    ``inplace=True`` (``sp_size == 1`` only) writes each result over its input
+    rows and returns ``[B, L, H, D]`` views of the inputs: every thread of the
+    kernel stores exactly the 16-byte chunks it loaded, after loading them, so
+    rows with any row stride (e.g. column slices of a fused QKV projection)
+    are safe to overwrite.
     """
     dev = _lib.require_cuda(*xs)
     B = int(xs[0].shape[0])
@@ -158,6 +164,8 @@ def norm_rope(xs, weights, pes, heads: int, dim_head: int, eps: float, sp_size: 
         if any(int(x.shape[1]) != L0 for x in xs):
             raise ValueError("packed send buffer needs equal lengths")
         buf = torch.empty(sp_size, B, L0, n, Hl, dim_head, device=dev, dtype=torch.bfloat16)
+    if inplace and (sp_size != 1 or packed or peer is not None):
+        raise ValueError("in-place norm_rope is for the unsharded layout only")
     jobs = (_lib.NormRopeJob * n)()
     keep = []
     outs = []
@@ -181,6 +189,11 @@ def norm_rope(xs, weights, pes, heads: int, dim_head: int, eps: float, sp_size: 
             outs.append(o)
             j.out = o.data_ptr()
             j.out_group_stride, j.out_batch_stride, j.out_row_stride = o.stride(0), o.stride(1), o.stride(2)
+        elif inplace:
+            o = x.view(B, L, heads, dim_head)
+            outs.append(o)
+            j.out = o.data_ptr()
+            j.out_group_stride, j.out_batch_stride, j.out_row_stride = 0, x.stride(0), x.stride(1)
         else:
             o = torch.empty(B, L, heads, dim_head, device=dev, dtype=torch.bfloat16)
             outs.append(o)

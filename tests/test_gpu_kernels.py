@@ -286,13 +286,19 @@ def make_attn(d):
     return attn
 
 
+@pytest.mark.parametrize("fused", [False, True], ids=["qkv3", "qkv_fused"])
 @pytest.mark.parametrize("case", list(inputs.ATTN_CASES))
-def test_attention_with_cache_vs_reference(golden_dir, case):
+def test_attention_with_cache_vs_reference(golden_dir, case, fused):
+    """Against the reference's fp32 outputs; ``qkv_fused`` runs the module
+    prepared by ``fuse_qkv_weights`` (one projection GEMM, q and k normalised
+    in place, strided new K/V)."""
     import taomate_b200 as tm
     z = np.load(os.path.join(golden_dir, f"attn_{case}.npz"))
     d = inputs.attn_case_inputs(case)
     c = d["cfg"]
     attn = make_attn(d)
+    if fused:
+        assert tm.fuse_qkv_weights(attn)
     x = _bf(d["x"])[None]
     pe = (_bf(z["cos_f32"])[None], _bf(z["sin_f32"])[None])
     ck = _bf(d["cached_k"])[None] if d["cached_k"] is not None else None

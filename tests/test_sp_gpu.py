@@ -83,6 +83,12 @@ def _worker(rank, world, port, outdir):
             out_p2, _, _ = tm.attention_with_cache(
                 attn, x2[:, ts].contiguous(), None, (cos[:, :, ts], sin[:, :, ts]), None,
                 ck[:, :, hs].contiguous(), cv[:, :, hs].contiguous())
+            out_p2 = out_p2.clone()
+            # one fused QKV GEMM: the kernel reads q/k/v as column slices
+            assert tm.fuse_qkv_weights(attn)
+            out_f, nk_f, nv_f = tm.attention_with_cache(
+                attn, x[:, ts].contiguous(), None, (cos[:, :, ts], sin[:, :, ts]), None,
+                ck[:, :, hs].contiguous(), cv[:, :, hs].contiguous())
         torch.cuda.synchronize()
         code = ctypes.c_int(0)
         assert _lib.load().tm_device_error(ctypes.byref(code)) == 0 and code.value == 0
@@ -90,7 +96,8 @@ def _worker(rank, world, port, outdir):
         f = lambda t: t.float().cpu().numpy()
         np.savez(os.path.join(outdir, f"r{rank}.npz"), out=f(out), ref_out=f(ref_out[:, ts]),
                  k=f(nk), ref_k=f(ref_k[:, :, hs]), v=f(nv), ref_v=f(ref_v[:, :, hs]),
-                 out_p=f(out_p), k_p=f(nk_p), v_p=f(nv_p), out_p2=f(out_p2))
+                 out_p=f(out_p), k_p=f(nk_p), v_p=f(nv_p), out_p2=f(out_p2), out_f=f(out_f),
+                 k_f=f(nk_f), v_f=f(nv_f))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -121,3 +128,6 @@ def test_ulysses_sp_matches_single_gpu(tmp_path, world):
         assert _rel_l2(z["out_p"], z["out"]) < 1e-3
         assert _rel_l2(z["k_p"], z["k"]) < 1e-3 and _rel_l2(z["v_p"], z["v"]) < 1e-3
         assert _rel_l2(z["out_p2"], z["out_p"]) > 1e-1  # the second call saw new inputs
+        # fused QKV projection: another GEMM kernel, the same arithmetic after it
+        assert _rel_l2(z["out_f"], z["out_p"]) < 1e-2
+        assert _rel_l2(z["k_f"], z["k_p"]) < 5e-3 and _rel_l2(z["v_f"], z["v_p"]) < 5e-3
