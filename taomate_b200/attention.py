@@ -402,12 +402,20 @@ def _projections(attn, x: Tensor, ctx: Tensor):
             F.linear(ctx, attn.to_v.weight, attn.to_v.bias))
 
 
-def _copy_kv(k: Tensor, v: Tensor) -> Tuple[Tensor, Tensor]:
-    """Contiguous copies of two ``[1, L, H, D]`` row-strided views in one
-    launch of the row-copy kernel."""
+_SIDE_STREAMS = {}
+
+
+def _side_stream(dev: torch.device) -> torch.cuda.Stream:
+    st = _SIDE_STREAMS.get(dev.index)
+    if st is None:
+        st = _SIDE_STREAMS[dev.index] = torch.cuda.Stream(dev)
+    return st
+
+
+def _copy_kv(k: Tensor, v: Tensor, outs: Tuple[Tensor, Tensor]) -> Tuple[Tensor, Tensor]:
+    """Contiguous copies of two ``[1, L, H, D]`` row-strided views into
+    ``outs`` in one launch of the row-copy kernel (current stream)."""
     dev = k.device
-    outs = (torch.empty(k.shape, dtype=k.dtype, device=dev),
-            torch.empty(v.shape, dtype=v.dtype, device=dev))
     row = int(k.shape[2]) * int(k.shape[3]) * k.element_size()
     spans = (_lib.CopySpan * 2)()
     for i, (src, dst) in enumerate(((k, outs[0]), (v, outs[1]))):
@@ -528,16 +536,25 @@ def attention_with_cache(
     # when the output rows stay on this rank
     fuse_gate = sp_size == 1 and getattr(attn, "to_gate_logits", None) is not None
     glog = attn.to_gate_logits(x) if fuse_gate else None
+    if peer is not None:
+        # The returned cache K/V must outlive the receive buffer, where the
+        # peers store the next call's rows once this rank has signalled the
+        # head->seq exchange.  They are copied out on a side stream, next to
+        # the attention kernel (which leaves a few SMs idle under sequence
+        # parallelism), and joined before the signal.
+        main, side = torch.cuda.current_stream(q.device), _side_stream(q.device)
+        kv_out = (torch.empty(k.shape, dtype=k.dtype, device=q.device),
+                  torch.empty(v.shape, dtype=v.dtype, device=q.device))
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            _copy_kv(k, v, kv_out)
     with section(base + ".sdpa"):
         out = flash_attention(q, ck, cv, spans, k, v, nk_rows, peer=peer, gate_logits=glog)
 
     # 5. head -> seq
     if peer is not None:
-        # The returned cache K/V must outlive the receive buffer: copy them
-        # before signalling, since after it the peers may store the next
-        # call's rows there.
-        with section(base + ".new_kv_copy"):
-            k, v = _copy_kv(k, v)
+        main.wait_stream(side)
+        k, v = kv_out
         with section(base + ".a2a_head2seq"):
             peer.exchange(1)
         out = peer.out

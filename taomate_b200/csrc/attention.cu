@@ -92,6 +92,7 @@ struct __align__(64) Params {
   int rows_per_rank;
   int head_base;
   int64_t out_delta[8];
+  int stage_out;  // some rows go to another rank: store whole rows through shared memory
   // Per-head output gate 2 * sigmoid(logit), logits [B, Lq, H] bf16 (head
   // stride 1), or null.
   const __nv_bfloat16* gate;
@@ -549,8 +550,44 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         s0 *= g;
         s1 *= g;
       }
-      __nv_bfloat16* orow = out_row(p.out, p.out_bs, p.out_rs, p.rows_per_rank, p.head_base,
-                                    p.out_delta, batch, qi, head, D);
+      if (!p.stage_out) {
+        // every row stays on this GPU: each thread stores its own row
+        __nv_bfloat16* orow = out_row(p.out, p.out_bs, p.out_rs, p.rows_per_rank, p.head_base,
+                                      p.out_delta, batch, qi, head, D);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32], o1[32];
+          TM_TMEM_LD32(tO + c * 32, o);
+          if (merge) {
+            TM_TMEM_LD32(tO1 + c * 32, o1);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o1[i] = 0u;
+          }
+          tmem_wait_ld();
+          if (qi < p.Lq) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              float f[8];
+#pragma unroll
+              for (int k = 0; k < 8; ++k)
+                f[k] = __uint_as_float(o[i + k]) * s0 + __uint_as_float(o1[i + k]) * s1;
+              const uint4 v = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                         pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+              *reinterpret_cast<uint4*>(orow + c * 32 + i) = v;
+            }
+          }
+        }
+      } else {
+      // Rows go to other GPUs: the warp's 32 rows x D bf16 go through a free
+      // Q buffer (split CTAs never load buffer 1; in a pair CTA this lane's
+      // own buffer, whose last MMA has completed), in 16-byte pieces
+      // XOR-swizzled by row, so that each warp store covers whole rows
+      // (32 / (D / 8) rows of 2 D contiguous bytes) instead of 32 scattered
+      // pieces, and crosses NVLink in full lines.
+      constexpr int kPieces = D / 8;
+      uint4* stg = reinterpret_cast<uint4*>(smem + C::kQOff + (split ? 1 : ln) * C::kQBytes) +
+                   q4 * 32 * kPieces;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32], o1[32];
@@ -562,18 +599,32 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           for (int i = 0; i < 32; ++i) o1[i] = 0u;
         }
         tmem_wait_ld();
-        if (qi < p.Lq) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            float f[8];
+        for (int i = 0; i < 32; i += 8) {
+          float f[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-              f[k] = __uint_as_float(o[i + k]) * s0 + __uint_as_float(o1[i + k]) * s1;
-            const uint4 v = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
-                                       pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
-            *reinterpret_cast<uint4*>(orow + c * 32 + i) = v;
-          }
+          for (int k = 0; k < 8; ++k)
+            f[k] = __uint_as_float(o[i + k]) * s0 + __uint_as_float(o1[i + k]) * s1;
+          const int pc = c * 4 + (i >> 3);
+          stg[lane_id * kPieces + (pc ^ (lane_id & (kPieces - 1)))] =
+              make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                         pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
         }
+      }
+      __syncwarp();
+      constexpr int kRowsPer = 32 / kPieces;
+      const int qw = qi - lane_id;  // the warp's first row
+      const int pc = lane_id % kPieces;
+#pragma unroll 4
+      for (int i = 0; i < 32 / kRowsPer; ++i) {
+        const int rr = i * kRowsPer + lane_id / kPieces;
+        if (qw + rr < p.Lq) {
+          __nv_bfloat16* orow = out_row(p.out, p.out_bs, p.out_rs, p.rows_per_rank, p.head_base,
+                                        p.out_delta, batch, qw + rr, head, D);
+          *reinterpret_cast<uint4*>(orow + pc * 8) =
+              stg[rr * kPieces + (pc ^ (rr & (kPieces - 1)))];
+        }
+      }
       }
       }
     }
@@ -888,6 +939,7 @@ static int attention_impl(const void* q, int64_t q_batch_stride, int64_t q_row_s
     if (ext.out_delta[i] & 15)
       return set_error(TM_ERR_ALIGNMENT, "attention: output offset %d not 16-byte aligned", i);
     prm.out_delta[i] = ext.out_delta[i];
+    if (ext.out_delta[i] != 0) prm.stage_out = 1;
   }
   if (ext.gate_logits) {
     if (ext.gate_row_stride < H || ext.gate_batch_stride < 0)

@@ -519,3 +519,36 @@ def test_attention_fused_gate(H):
     refb = _sdpa_bf16(q, [k], [v]).float() * g
     assert torch.isfinite(out).all()
     assert rel_l2(out, ref) < 1.02 * rel_l2(refb, ref) + 1e-4
+
+
+@pytest.mark.parametrize("H", [32, 16, 4])
+def test_attention_output_placement_across_rank_buffers(H):
+    """The head->seq placement of the fused exchange, on one GPU: query rows
+    [r * S, (r + 1) * S) land in "rank" r's buffer [1, S, 2 H, D] at heads
+    [H, 2 H), through the per-rank byte offsets (here two local buffers
+    instead of a local and a peer-mapped one).  That switches the epilogue to
+    whole-row stores through shared memory (pair CTAs and the odd tile's
+    split CTA at 32 heads, split CTAs at 16, the key-range merge at 4); the
+    rows must equal the plain call's bit for bit."""
+    from types import SimpleNamespace
+    from taomate_b200 import flash_attention
+    gen = torch.Generator().manual_seed(31 + H)
+    D, Lq, Lc = 128, 1152, 3456
+    S = Lq // 2
+    q = torch.randn(1, Lq, H, D, generator=gen).to(DEV, torch.bfloat16)
+    ck = torch.randn(1, Lc, H, D, generator=gen).to(DEV, torch.bfloat16)
+    cv = torch.randn(1, Lc, H, D, generator=gen).to(DEV, torch.bfloat16)
+    nk = torch.randn(1, Lq, H, D, generator=gen).to(DEV, torch.bfloat16)
+    nv = torch.randn(1, Lq, H, D, generator=gen).to(DEV, torch.bfloat16)
+    ref = flash_attention(q, ck, cv, [(0, Lc)], nk, nv, Lq)
+    bufs = [torch.full((1, S, 2 * H, D), float("nan"), device=DEV, dtype=torch.bfloat16)
+            for _ in range(2)]
+    own = bufs[1]  # this "rank" is rank 1: its heads sit at [H, 2 H) of every buffer
+    delta = [b.data_ptr() - own.data_ptr() for b in bufs] + [0] * 6
+    peer = SimpleNamespace(sp=2, S_loc=S, Hl=H, D=D, B=1, rank=1, out=own,
+                           delta={"out": delta})
+    flash_attention(q, ck, cv, [(0, Lc)], nk, nv, Lq, peer=peer)
+    torch.cuda.synchronize()
+    for r in range(2):
+        assert torch.equal(bufs[r][:, :, H:], ref[:, r * S:(r + 1) * S])
+        assert torch.isnan(bufs[r][:, :, :H].float()).all()  # other ranks' heads untouched
