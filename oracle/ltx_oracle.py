@@ -333,6 +333,39 @@ def text_cross_attention(x: np.ndarray, context: np.ndarray, params: Dict[str, n
     return np.stack(outs)
 
 
+def cross_modal_pair_attention(a2v_params: Dict[str, np.ndarray], v2a_params: Dict[str, np.ndarray],
+                               heads: int, dim_head: int, vx_a2v: np.ndarray, ax_a2v: np.ndarray,
+                               ax_v2a: np.ndarray, vx_v2a: np.ndarray,
+                               video_cross_pe: Tuple[np.ndarray, np.ndarray],
+                               audio_cross_pe: Tuple[np.ndarray, np.ndarray],
+                               a2v_cache=None, v2a_cache=None,
+                               video_real_len: Optional[int] = None,
+                               audio_real_len: Optional[int] = None, eps: float = 1e-6,
+                               dtype=np.float64):
+    """Paired A2V / V2A attention on one rank
+    (``_cross_modal_pair_attention_with_cache``,
+    ltx_causal/transformer/kv_cache.py:1967-2138).  The pairing only packs the
+    two attentions' all-to-alls; each is the cached attention of
+    ``attention_with_cache`` with a context: A2V takes queries from video
+    (video cross RoPE) and keys from audio (audio cross RoPE) against the
+    ``a2v`` cache, keeping ``audio_real_len`` new keys; V2A the reverse
+    against the ``v2a`` cache (``_project_qkv_local_for_cross_pair`` :1550-1597,
+    ``_finish_attention_from_head_layout`` :1600-1651).  Caches are
+    ``(k, v)`` pairs of ``[L, H, D]`` or None.  Returns
+    ``(a2v_out, a2v_k, a2v_v, v2a_out, v2a_k, v2a_v)``.
+    """
+    ck = lambda c, i: None if c is None else c[i]
+    a2v = attention_with_cache(vx_a2v, a2v_params, heads, dim_head, video_cross_pe,
+                               ck(a2v_cache, 0), ck(a2v_cache, 1), context=ax_a2v,
+                               k_pe=audio_cross_pe, new_kv_real_len=audio_real_len, eps=eps,
+                               dtype=dtype)
+    v2a = attention_with_cache(ax_v2a, v2a_params, heads, dim_head, audio_cross_pe,
+                               ck(v2a_cache, 0), ck(v2a_cache, 1), context=vx_v2a,
+                               k_pe=video_cross_pe, new_kv_real_len=video_real_len, eps=eps,
+                               dtype=dtype)
+    return a2v + v2a
+
+
 # ----------------------------------------------------------------------------
 # A4 / A8 / A13: Ulysses layout permutations (global view over all ranks)
 # ----------------------------------------------------------------------------

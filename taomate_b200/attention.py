@@ -572,6 +572,48 @@ def attention_with_cache(
     return out, k, v
 
 
+def cross_modal_pair_attention_with_cache(
+    audio_to_video_attn,
+    video_to_audio_attn,
+    vx_a2v: Tensor,
+    ax_a2v: Tensor,
+    ax_v2a: Tensor,
+    vx_v2a: Tensor,
+    video_cross_pe: Optional[Tuple[Tensor, Tensor]],
+    audio_cross_pe: Optional[Tuple[Tensor, Tensor]],
+    layer_cache,
+    *,
+    video_real_len: Optional[int],
+    audio_real_len: Optional[int],
+    layer_idx: Optional[int],
+):
+    """Paired A2V / V2A attention with cache (kv_cache.py:1967-2138).
+
+    A2V: queries from video (``vx_a2v``, video cross RoPE), keys and values
+    from audio (``ax_a2v``, audio cross RoPE), cached in
+    ``layer_cache.a2v_k/v``; ``audio_real_len`` new rows are kept.  V2A is
+    the reverse, cached in ``layer_cache.v2a_k/v``, keeping ``video_real_len``
+    rows.  The two attentions are independent until the caller's residual
+    updates.  The reference pairs them only to pack their same-shaped
+    all-to-alls.  Here each one is an ``attention_with_cache`` call with a
+    context: the same kernels, with each call's Q, K and V packed into its
+    own exchange.  Returns ``(a2v_out, new_a2v_k, new_a2v_v, v2a_out,
+    new_v2a_k, new_v2a_v)``.
+    """
+    a2v = attention_with_cache(audio_to_video_attn, vx_a2v, ax_a2v, video_cross_pe,
+                               audio_cross_pe, layer_cache.a2v_k, layer_cache.a2v_v,
+                               layer_idx=layer_idx, new_kv_real_len=audio_real_len,
+                               profile_name="attn.audio_to_video")
+    v2a = attention_with_cache(video_to_audio_attn, ax_v2a, vx_v2a, audio_cross_pe,
+                               video_cross_pe, layer_cache.v2a_k, layer_cache.v2a_v,
+                               layer_idx=layer_idx, new_kv_real_len=video_real_len,
+                               profile_name="attn.video_to_audio")
+    return a2v + v2a
+
+
+_cross_modal_pair_attention_with_cache = cross_modal_pair_attention_with_cache
+
+
 class AttentionWeights(torch.nn.Module):
     """Weight container with the attribute names of the reference's
     ``CausalLTXAttention`` (ltx_causal/attention/causal_attention.py:55-118):

@@ -102,6 +102,59 @@ def text_cross_inputs(name: str) -> dict:
     return dict(cfg=c, params=p, x=x, context=context, mask=mask)
 
 
+# Paired A2V / V2A cross-modal attention (kv_cache.py:1967-2138): video
+# queries against audio keys and audio queries against video keys, both with
+# 1-D temporal cross RoPE and their own caches.
+PAIR_CASES: Dict[str, dict] = {
+    # 2 video frames of 48 tokens, 25 audio tokens, both caches filled.
+    "av": dict(v_hidden=384, a_hidden=256, heads=4, dim_head=64, v_frames=2, frame_seqlen=48,
+               la=25, a2v_cache=50, v2a_cache=96, v_start=3, a_start=75, gated=(False, True),
+               video_real_len=None, audio_real_len=None, seed=20),
+    # Audio padded to 28 rows (as under sequence parallelism), real length 25;
+    # empty caches (first block).
+    "strip": dict(v_hidden=256, a_hidden=256, heads=4, dim_head=64, v_frames=1, frame_seqlen=96,
+                  la=28, a2v_cache=0, v2a_cache=0, v_start=0, a_start=0, gated=(True, False),
+                  video_real_len=None, audio_real_len=25, seed=21),
+}
+
+
+def _pair_attn_params(rng, q_dim, kv_dim, inner, heads, gated):
+    p = {}
+    for nm, (o, i) in {"to_q": (inner, q_dim), "to_k": (inner, kv_dim), "to_v": (inner, kv_dim),
+                       "to_out": (q_dim, inner)}.items():
+        p[nm + "_w"] = (rng.standard_normal((o, i)) * 0.02).astype(np.float32)
+        p[nm + "_b"] = (rng.standard_normal(o) * 0.02).astype(np.float32)
+    if gated:
+        p["to_gate_logits_w"] = (rng.standard_normal((heads, q_dim)) * 0.02).astype(np.float32)
+        p["to_gate_logits_b"] = (rng.standard_normal(heads) * 0.02).astype(np.float32)
+    p["q_norm_w"] = rng.uniform(0.5, 1.5, inner).astype(np.float32)
+    p["k_norm_w"] = rng.uniform(0.5, 1.5, inner).astype(np.float32)
+    return p
+
+
+def pair_case_inputs(name: str) -> dict:
+    """Seeded inputs of a paired cross-modal case: the A2V module (queries
+    from video, keys from audio) and the V2A module, the four normed inputs
+    ``vx_a2v [Lv, Dv]``, ``ax_a2v [La, Da]``, ``ax_v2a``, ``vx_v2a`` and the
+    caches (``a2v`` holds audio keys, ``v2a`` video keys; ``None`` when empty)."""
+    c = PAIR_CASES[name]
+    rng = np.random.default_rng(3000 + c["seed"])
+    H, D = c["heads"], c["dim_head"]
+    inner = H * D
+    lv = c["v_frames"] * c["frame_seqlen"]
+    a2v = _pair_attn_params(rng, c["v_hidden"], c["a_hidden"], inner, H, c["gated"][0])
+    v2a = _pair_attn_params(rng, c["a_hidden"], c["v_hidden"], inner, H, c["gated"][1])
+    x = {nm: rng.standard_normal((n, dim)).astype(np.float32)
+         for nm, n, dim in (("vx_a2v", lv, c["v_hidden"]), ("ax_a2v", c["la"], c["a_hidden"]),
+                            ("ax_v2a", c["la"], c["a_hidden"]), ("vx_v2a", lv, c["v_hidden"]))}
+    caches = {}
+    for nm in ("a2v", "v2a"):
+        n = c[nm + "_cache"]
+        caches[nm] = None if n == 0 else tuple(
+            rng.standard_normal((n, H, D)).astype(np.float32) for _ in range(2))
+    return dict(cfg=c, a2v=a2v, v2a=v2a, x=x, caches=caches, lv=lv)
+
+
 def split_rope_inputs() -> np.ndarray:
     """x ``[96, 256]`` for the split-RoPE case (C1 shapes)."""
     return np.random.default_rng(77).standard_normal((96, 256)).astype(np.float32)

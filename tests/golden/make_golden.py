@@ -2,7 +2,7 @@
 
 Run once in a container where the reference source tree is available:
 
-    TAOMATE_REFERENCE=/path/to/TaoMate python tests/golden/make_golden.py
+    TAOMATE_REFERENCE=/path/to/TaoMate python tests/golden/make_golden.py [group ...]
 
 The reference is pure PyTorch; this script imports it, feeds it seeded inputs
 and stores the outputs as small ``.npz``/``.json`` files next to this script
@@ -160,6 +160,66 @@ def gen_text_cross(CausalLTXAttention, kv_cache, torch):
         np.savez_compressed(os.path.join(HERE, f"text_cross_{name}.npz"), **rec)
 
 
+def _load_module(attn, prm, torch):
+    with torch.no_grad():
+        mods = {"to_q": attn.to_q, "to_k": attn.to_k, "to_v": attn.to_v,
+                "to_out": attn.to_out[0]}
+        if attn.to_gate_logits is not None:
+            mods["to_gate_logits"] = attn.to_gate_logits
+        for nm, m in mods.items():
+            m.weight.copy_(torch.from_numpy(prm[nm + "_w"]))
+            m.bias.copy_(torch.from_numpy(prm[nm + "_b"]))
+        attn.q_norm.weight.copy_(torch.from_numpy(prm["q_norm_w"]))
+        attn.k_norm.weight.copy_(torch.from_numpy(prm["k_norm_w"]))
+
+
+def gen_pair(causal_rope, CausalLTXAttention, kv_cache, torch):
+    """_cross_modal_pair_attention_with_cache (kv_cache.py:1967-2138) on one
+    rank, fp32 and bf16, with the cross RoPE tables built as
+    kv_cache.py:2955-2990 builds them (1-D temporal tables, the video one
+    repeated per frame token)."""
+    for name in inputs.PAIR_CASES:
+        d = inputs.pair_case_inputs(name)
+        c = d["cfg"]
+        H, D = c["heads"], c["dim_head"]
+        inner = H * D
+        a2v = CausalLTXAttention(c["v_hidden"], c["a_hidden"], heads=H, dim_head=D,
+                                 apply_gated_attention=c["gated"][0])
+        v2a = CausalLTXAttention(c["a_hidden"], c["v_hidden"], heads=H, dim_head=D,
+                                 apply_gated_attention=c["gated"][1])
+        _load_module(a2v, d["a2v"], torch)
+        _load_module(v2a, d["v2a"], torch)
+        vc, vs = causal_rope.causal_precompute_freqs_cis(
+            torch.tensor([[c["v_frames"]]]), inner, max_pos=[20], start_frame=c["v_start"],
+            device="cpu", is_audio=False, num_attention_heads=H)
+        fs = c["frame_seqlen"]
+        expand = lambda t: t.unsqueeze(3).expand(-1, -1, -1, fs, -1).reshape(
+            t.shape[0], t.shape[1], t.shape[2] * fs, t.shape[3])
+        vc, vs = expand(vc), expand(vs)
+        ac, as_ = causal_rope.causal_precompute_freqs_cis(
+            torch.tensor([[c["la"]]]), inner, max_pos=[20], start_frame=c["a_start"],
+            device="cpu", is_audio=True, num_attention_heads=H)
+        rec = {"vcos_f32": f32(vc[0]), "vsin_f32": f32(vs[0]), "acos_f32": f32(ac[0]),
+               "asin_f32": f32(as_[0])}
+        for tag, dt in (("f32", torch.float32), ("bf16", torch.bfloat16)):
+            t = lambda a: None if a is None else torch.from_numpy(a)[None].to(dt)
+            cache = kv_cache.LayerKVCache()
+            for nm in ("a2v", "v2a"):
+                kv = d["caches"][nm]
+                if kv is not None:
+                    setattr(cache, nm + "_k", t(kv[0]))
+                    setattr(cache, nm + "_v", t(kv[1]))
+            with torch.no_grad():
+                outs = kv_cache._cross_modal_pair_attention_with_cache(
+                    a2v.to(dt), v2a.to(dt), t(d["x"]["vx_a2v"]), t(d["x"]["ax_a2v"]),
+                    t(d["x"]["ax_v2a"]), t(d["x"]["vx_v2a"]), (vc.to(dt), vs.to(dt)),
+                    (ac.to(dt), as_.to(dt)), cache, video_real_len=c["video_real_len"],
+                    audio_real_len=c["audio_real_len"], layer_idx=0)
+            for key, o in zip(("a2v_out", "a2v_k", "a2v_v", "v2a_out", "v2a_k", "v2a_v"), outs):
+                rec[f"{key}_{tag}"] = f32(o[0])
+        np.savez_compressed(os.path.join(HERE, f"pair_{name}.npz"), **rec)
+
+
 def gen_attention(causal_rope, CausalLTXAttention, kv_cache, torch):
     for name in inputs.ATTN_CASES:
         _attn_case(causal_rope, CausalLTXAttention, kv_cache, torch, name)
@@ -272,12 +332,17 @@ def main():
     causal_rope, CausalLTXAttention, kv_cache, tcache, compute_av_blocks = _import_reference()
     import torch
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    gen_rope(causal_rope, torch)
-    gen_split_rope(causal_rope, torch)
-    gen_attention(causal_rope, CausalLTXAttention, kv_cache, torch)
-    gen_text_cross(CausalLTXAttention, kv_cache, torch)
-    gen_cache(kv_cache, tcache, torch, compute_av_blocks)
-    gen_a2a()
+    groups = {
+        "rope": lambda: gen_rope(causal_rope, torch),
+        "split_rope": lambda: gen_split_rope(causal_rope, torch),
+        "attention": lambda: gen_attention(causal_rope, CausalLTXAttention, kv_cache, torch),
+        "text_cross": lambda: gen_text_cross(CausalLTXAttention, kv_cache, torch),
+        "pair": lambda: gen_pair(causal_rope, CausalLTXAttention, kv_cache, torch),
+        "cache": lambda: gen_cache(kv_cache, tcache, torch, compute_av_blocks),
+        "a2a": gen_a2a,
+    }
+    for name in (sys.argv[1:] or list(groups)):  # e.g. `make_golden.py pair`
+        groups[name]()
     import einops
     with open(os.path.join(HERE, "versions.json"), "w") as fh:
         json.dump({"torch": torch.__version__, "numpy": np.__version__,

@@ -316,6 +316,41 @@ def test_attention_with_cache_vs_reference(golden_dir, case, fused):
     assert rel_l2(nv[0], z["new_v_f32"]) < 1.25 * rel_l2(z["new_v_bf16"], z["new_v_f32"])
 
 
+@pytest.mark.parametrize("case", list(inputs.PAIR_CASES))
+def test_cross_modal_pair_vs_reference(golden_dir, case):
+    """Paired A2V / V2A attention (video queries over cached audio keys and the
+    reverse, 1-D cross RoPE, D = 64, one gated side, a padded audio strip)
+    against the reference's fp32 outputs, with the same bar as
+    ``attention_with_cache``: no worse than 1.25x the reference's own bf16
+    run."""
+    import taomate_b200 as tm
+    from taomate_b200.kv_cache import LayerKVCache
+    z = np.load(os.path.join(golden_dir, f"pair_{case}.npz"))
+    d = inputs.pair_case_inputs(case)
+    c = d["cfg"]
+    mk = lambda prm, gated: make_attn({"cfg": {"heads": c["heads"], "dim_head": c["dim_head"],
+                                               "gated": gated}, "params": prm})
+    a2v, v2a = mk(d["a2v"], c["gated"][0]), mk(d["v2a"], c["gated"][1])
+    cache = LayerKVCache()
+    for nm in ("a2v", "v2a"):
+        kv = d["caches"][nm]
+        if kv is not None:
+            setattr(cache, nm + "_k", _bf(kv[0])[None])
+            setattr(cache, nm + "_v", _bf(kv[1])[None])
+    vpe = (_bf(z["vcos_f32"])[None], _bf(z["vsin_f32"])[None])
+    ape = (_bf(z["acos_f32"])[None], _bf(z["asin_f32"])[None])
+    x = {k: _bf(v)[None] for k, v in d["x"].items()}
+    with torch.no_grad():
+        outs = tm.cross_modal_pair_attention_with_cache(
+            a2v, v2a, x["vx_a2v"], x["ax_a2v"], x["ax_v2a"], x["vx_v2a"], vpe, ape, cache,
+            video_real_len=c["video_real_len"], audio_real_len=c["audio_real_len"], layer_idx=0)
+    keys = ("a2v_out", "a2v_k", "a2v_v", "v2a_out", "v2a_k", "v2a_v")
+    for key, o in zip(keys, outs):
+        ref, refb = z[f"{key}_f32"], z[f"{key}_bf16"]
+        assert tuple(o.shape) == (1,) + ref.shape, key
+        assert rel_l2(o[0], ref) < 1.25 * rel_l2(refb, ref), key
+
+
 @pytest.mark.parametrize("case", list(inputs.TEXT_CROSS_CASES))
 def test_text_cross_attention_vs_reference(golden_dir, case):
     """Text cross-attention with cached K/V and the prompt's padding mask

@@ -106,6 +106,28 @@ def test_text_cross_attention_matches_reference(golden_dir, case):
     assert rel_l2(out, z["out_bf16"]) < 2e-2  # the reference's own bf16 path
 
 
+PAIR_KEYS = ("a2v_out", "a2v_k", "a2v_v", "v2a_out", "v2a_k", "v2a_v")
+
+
+@pytest.mark.parametrize("case", list(inputs.PAIR_CASES))
+def test_cross_modal_pair_matches_reference(golden_dir, case):
+    """The paired A2V / V2A attention equals two cached cross attentions."""
+    z = _load(golden_dir, f"pair_{case}.npz")
+    d = inputs.pair_case_inputs(case)
+    c = d["cfg"]
+    got = O.cross_modal_pair_attention(
+        d["a2v"], d["v2a"], c["heads"], c["dim_head"], d["x"]["vx_a2v"], d["x"]["ax_a2v"],
+        d["x"]["ax_v2a"], d["x"]["vx_v2a"], (z["vcos_f32"], z["vsin_f32"]),
+        (z["acos_f32"], z["asin_f32"]), d["caches"]["a2v"], d["caches"]["v2a"],
+        video_real_len=c["video_real_len"], audio_real_len=c["audio_real_len"])
+    for key, g in zip(PAIR_KEYS, got):
+        ref = z[f"{key}_f32"]
+        assert g.shape == ref.shape, key
+        assert rel_l2(g, ref) < 2e-5, key
+        # the reference's bf16 run, for scale
+        assert rel_l2(g, z[f"{key}_bf16"]) < 2e-2, key
+
+
 def test_av_blocks_known_answers(golden_dir):
     with open(os.path.join(golden_dir, "av_blocks.json")) as fh:
         kab = json.load(fh)
