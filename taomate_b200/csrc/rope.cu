@@ -136,8 +136,12 @@ __device__ __forceinline__ void unpack8(const uint4& v, float* f) {
   }
 }
 
+// At least 6 blocks per SM (79 registers at H*D = 4096 instead of 96, no
+// spills): one more row in flight per SM; measured 19.8 vs 21.8 us per call
+// in the C2 step.
 template <int D, int CPT, int TPR>
-__global__ void __launch_bounds__(TPR) norm_rope_kernel(const __grid_constant__ NormRopeParams p) {
+__global__ void __launch_bounds__(TPR, 6)
+    norm_rope_kernel(const __grid_constant__ NormRopeParams p) {
   constexpr int kChunksPerHead = D / 8;
   constexpr int kHalf = D / 16;
   constexpr int kInner = CPT * TPR * 8;
