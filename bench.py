@@ -229,7 +229,7 @@ def run_ours(args):
     from taomate_b200 import _lib, parallel as P
     from taomate_b200.attention import AttentionWeights
     from taomate_b200.cache import retain_window
-    from taomate_b200.graphs import AttentionGraph, attention_spans, copy_into
+    from taomate_b200.graphs import AttentionGraph, attention_spans, copy_bytes, copy_into
     from taomate_b200.kv_cache import ArenaSpec, KVCache, LayerKVCache, init_arena_cache
     from taomate_b200.profiler import TIMER
 
@@ -299,6 +299,8 @@ def run_ours(args):
         return (cos[:, :, rank * S_loc:(rank + 1) * S_loc],
                 sin[:, :, rank * S_loc:(rank + 1) * S_loc])
 
+    read_stream = torch.cuda.Stream(dev)  # output read-back of the graph runners
+
     class GraphRunner:
         """One captured 48-layer forward (all four forwards of a block are the
         same computation over the same cache: the commit forward only keeps its
@@ -326,6 +328,27 @@ def run_ours(args):
                 return out, kv
 
             self.out, self.kv = self.graph.capture(forward)
+            # read-back: a kernel copy into one of two device buffers on the
+            # compute stream, then the device-to-host copy on the read-back
+            # stream, so that the next forward does not wait for PCIe
+            self.stage = [torch.empty_like(self.out) for _ in range(2)]
+            self.read_done = [None, None]
+
+        def read_back(self, fwd, host):
+            i = fwd % 2
+            main = torch.cuda.current_stream(dev)
+            if self.read_done[i] is not None:
+                main.wait_event(self.read_done[i])  # that buffer's previous copy has left
+            copy_bytes(self.stage[i].data_ptr(), self.out.data_ptr(),
+                       self.out.numel() * self.out.element_size(), dev)
+            ready = torch.cuda.Event()
+            ready.record(main)
+            read_stream.wait_event(ready)
+            with torch.cuda.stream(read_stream):
+                host.copy_(self.stage[i], non_blocking=True)
+                done = torch.cuda.Event()
+                done.record(read_stream)
+            self.read_done[i] = done
 
         def step(self, cache, block, outs=None):
             c, s = tables(block)  # once per block: the four forwards share the start frame
@@ -336,7 +359,7 @@ def run_ours(args):
             for fwd in range(FORWARDS_PER_STEP):
                 self.graph.replay(spans if fwd == 0 else None)
                 if outs is not None:
-                    outs[fwd].copy_(self.out, non_blocking=True)
+                    self.read_back(fwd, outs[fwd])
             new_layers = []
             for li, lay in enumerate(cache.layers):
                 nk, nv = self.kv[li]
@@ -415,6 +438,8 @@ def run_ours(args):
                 else:
                     cache = step(cache, block)
                 block += 1
+            # the timed region ends once the last read-back has reached the host
+            torch.cuda.current_stream(dev).wait_stream(read_stream)
         e1.record()
         torch.cuda.synchronize()
         clocks = sampler.stop()
