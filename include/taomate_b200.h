@@ -127,7 +127,9 @@ TM_API int tm_norm_rope_peer(const tm_norm_rope_job* jobs, int n_jobs, int B, in
  *                   rank i's flag buffer as mapped here);
  *   tm_peer_wait    stream-ordered wait until every rank published that epoch;
  *                   gives up after 2 s and records device error 2
- *                   (tm_device_error) instead of hanging.
+ *                   (tm_device_error) instead of hanging;
+ *   tm_peer_exchange  tm_peer_signal then tm_peer_wait in one kernel launch
+ *                   (flags = this rank's own flag buffer).
  * At most 8 ranks.  Plain peer stores and loads; no multicast.
  */
 TM_API int tm_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle);
@@ -138,6 +140,8 @@ TM_API int64_t tm_peer_flag_bytes(void);
 TM_API int tm_peer_signal(void* const* peer_flags, int n_ranks, int rank, void* counters, int slot,
                    void* stream);
 TM_API int tm_peer_wait(const void* flags, int n_ranks, void* counters, int slot, void* stream);
+TM_API int tm_peer_exchange(void* const* peer_flags, int n_ranks, int rank, const void* flags,
+                     void* counters, int slot, void* stream);
 
 /*
  * A6/A11/A12. Row-span copies for the KV slot arena: commit-time append of a

@@ -9,7 +9,8 @@
 //   tm_peer_wait    one thread spins (acquire loads, bounded by 2 s of
 //                   %globaltimer) until every rank's flag reached this rank's
 //                   next epoch; on timeout it records TM device error 2 and
-//                   returns, so a lost peer never hangs the GPU.
+//                   returns, so a lost peer never hangs the GPU;
+//   tm_peer_exchange  both in one launch.
 // Epochs are counted on the device (per slot), so the same launches can be
 // replayed from a CUDA graph.  Plain peer loads/stores only: no multicast,
 // no NVLS.
@@ -51,9 +52,10 @@ __global__ void signal_kernel(const __grid_constant__ SignalParams p) {
   }
 }
 
-__global__ void wait_kernel(const unsigned long long* flags, unsigned long long* counters,
-                            int n_ranks, int slot, int* err) {
-  if (threadIdx.x != 0) return;
+// Thread 0 waits until every rank's flag of `slot` reached this rank's next
+// awaited epoch (bounded; device error kDevPeerTimeout on giving up).
+__device__ void wait_flags(const unsigned long long* flags, unsigned long long* counters,
+                           int n_ranks, int slot, int* err) {
   const unsigned long long target = ++counters[kSlots + slot];
   const unsigned long long* f = flags + slot * kMaxRanks;
   const unsigned long long t0 = globaltimer_ns();
@@ -69,6 +71,29 @@ __global__ void wait_kernel(const unsigned long long* flags, unsigned long long*
     }
   }
   asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+__global__ void wait_kernel(const unsigned long long* flags, unsigned long long* counters,
+                            int n_ranks, int slot, int* err) {
+  if (threadIdx.x == 0) wait_flags(flags, counters, n_ranks, slot, err);
+}
+
+// signal_kernel then wait_kernel in one launch: a replayed graph pays one
+// node instead of two per exchange.
+__global__ void exchange_kernel(const __grid_constant__ SignalParams p,
+                                const unsigned long long* flags, int* err) {
+  __shared__ unsigned long long epoch;
+  if (threadIdx.x == 0) {
+    epoch = ++p.counters[p.slot];
+    asm volatile("fence.sc.sys;" ::: "memory");
+  }
+  __syncthreads();
+  const int g = threadIdx.x;
+  if (g < p.n_ranks) {
+    unsigned long long* f = p.peer_flags[g] + p.slot * kMaxRanks + p.rank;
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(epoch) : "memory");
+  }
+  if (threadIdx.x == 0) wait_flags(flags, p.counters, p.n_ranks, p.slot, err);
 }
 
 }  // namespace peer
@@ -145,6 +170,29 @@ extern "C" int tm_peer_wait(const void* flags, int n_ranks, void* counters, int 
       static_cast<const unsigned long long*>(flags), static_cast<unsigned long long*>(counters),
       n_ranks, slot, err);
   return check_cuda(cudaGetLastError(), "peer_wait: launch");
+}
+
+extern "C" int tm_peer_exchange(void* const* peer_flags, int n_ranks, int rank, const void* flags,
+                                void* counters, int slot, void* stream) {
+  using namespace tmb::peer;
+  if (n_ranks < 1 || n_ranks > kMaxRanks || rank < 0 || rank >= n_ranks || slot < 0 ||
+      slot >= kSlots || !peer_flags || !flags || !counters)
+    return set_error(TM_ERR_INVALID_ARGUMENT, "peer_exchange: bad arguments");
+  int* err = device_error_flag();
+  if (!err) return set_error(TM_ERR_CUDA, "peer_exchange: device error flag unavailable");
+  SignalParams p;
+  memset(&p, 0, sizeof(p));
+  for (int g = 0; g < n_ranks; ++g) {
+    if (!peer_flags[g]) return set_error(TM_ERR_INVALID_ARGUMENT, "peer_exchange: null flags");
+    p.peer_flags[g] = static_cast<unsigned long long*>(peer_flags[g]);
+  }
+  p.counters = static_cast<unsigned long long*>(counters);
+  p.n_ranks = n_ranks;
+  p.rank = rank;
+  p.slot = slot;
+  exchange_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      p, static_cast<const unsigned long long*>(flags), err);
+  return check_cuda(cudaGetLastError(), "peer_exchange: launch");
 }
 
 extern "C" int64_t tm_peer_flag_bytes(void) {

@@ -477,11 +477,10 @@ class PeerExchange:
     def exchange(self, slot: int) -> None:
         """Publish this rank's stores of ``slot`` and wait for every rank's."""
         stream = _lib.stream_ptr(self.device)
-        _lib.check(self.lib.tm_peer_signal(self._flag_ptrs, self.sp, self.rank, self._counters,
-                                           slot, stream), "peer_signal")
-        _lib.check(self.lib.tm_peer_wait(self._own["flags"], self.sp, self._counters, slot,
-                                         stream), "peer_wait")
-        _lib.launched(2)
+        _lib.check(self.lib.tm_peer_exchange(self._flag_ptrs, self.sp, self.rank,
+                                             self._own["flags"], self._counters, slot, stream),
+                   "peer_exchange")
+        _lib.launched()
 
     def close(self) -> None:
         if not self._own:
