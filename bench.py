@@ -31,7 +31,6 @@ import datetime
 import json
 import math
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -142,15 +141,19 @@ def measured_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def profiled_traffic():
-    """Per-launch DRAM bytes of the attention kernel from the committed ncu
-    summary (profiles/attention_c2.md), or None."""
-    p = os.path.join(ROOT, "profiles", "attention_c2.md")
+def profiled_traffic(kernel: str, heads: int):
+    """DRAM bytes per launch of ``kernel`` at ``heads`` heads per GPU from the
+    committed ncu capture table (profiles/traffic.json), or None when that
+    launch shape was not captured."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
     if not os.path.exists(p):
         return None
     with open(p) as fh:
-        m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", fh.read())
-    return float(m.group(1)) if m else None
+        table = json.load(fh).get(kernel, {})
+    for ent in table.values():
+        if int(ent.get("heads", -1)) == heads:
+            return float(ent["dram_bytes_per_launch"])
+    return None
 
 
 # --------------------------------------------------------------------------- CPU
@@ -446,11 +449,15 @@ def run_ours(args):
         TIMER.stop()
         launches = _lib.LAUNCHES - l0
         ms = e0.elapsed_time(e1)
+        # a bounded device wait that ran out (a lost peer, a stuck pipeline)
+        # would leave stale rows behind: read the flag after every pass
+        derr = _lib.device_error()
         if world > 1:
-            t = torch.tensor([ms], device=dev)
+            t = torch.tensor([ms, float(derr)], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+            ms, derr = float(t[0].item()), int(t[1].item())
             dist.barrier()
+        DEVICE_ERRORS.append(derr)
         h2d = sum(x.numel() * x.element_size() for x in xs) if host_io else 0
         d2h = FORWARDS_PER_STEP * S_loc * HIDDEN * 2 if host_io else 0
         for r in runners:
@@ -459,6 +466,7 @@ def run_ours(args):
         runner = None
         return ms, launches, clocks, h2d, d2h
 
+    DEVICE_ERRORS = []
     graphed = not args.eager
     ms, launches, clocks, _, _ = timed(args.steps, args.warmup, host_io=False, graphed=graphed)
     value = Q_FRAMES * args.steps / (ms / 1e3)
@@ -483,10 +491,7 @@ def run_ours(args):
     if sd:
         achieved = flops / (sd["mean_ms"] * 1e-3) / 1e12
         peak = float(peaks["bf16_tflops_sustained"])
-        traffic = profiled_traffic()
-        if traffic is not None and H_loc != HEADS:
-            # the capture is the 32-head launch; per-head bytes (Q, K/V, out) scale with heads
-            traffic = traffic * H_loc / HEADS
+        traffic = profiled_traffic("attn_fwd_kernel<128>", H_loc)
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "traffic": traffic,
                 "kernel": "tm attention (tcgen05)", "launch_ms": sd["mean_ms"],
@@ -523,6 +528,7 @@ def run_ours(args):
                              "activations, ~14 GB), no flush"},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clocks,
+            "device_error": max(DEVICE_ERRORS),
             "sections_ms_per_call": {k: v["mean_ms"] for k, v in sections.items()},
         }
         print(json.dumps(line), flush=True)

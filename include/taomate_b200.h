@@ -46,7 +46,8 @@ TM_API const char* tm_last_error(void);
 /*
  * Read and clear the device-side error flag of the current device.  Blocks
  * until all prior work on the device has finished.  *code_out receives 0 when
- * no kernel reported an error, 1 when a bounded wait ran out.
+ * no kernel reported an error, 1 when an attention kernel's bounded pipeline
+ * wait ran out, 2 when a peer flag wait (tm_peer_wait / tm_peer_exchange) did.
  */
 TM_API int tm_device_error(int* code_out);
 
@@ -126,10 +127,15 @@ TM_API int tm_norm_rope_peer(const tm_norm_rope_job* jobs, int n_jobs, int B, in
  *                   `slot` (0..3) in every rank's flag buffer (peer_flags[i] =
  *                   rank i's flag buffer as mapped here);
  *   tm_peer_wait    stream-ordered wait until every rank published that epoch;
- *                   gives up after 2 s and records device error 2
- *                   (tm_device_error) instead of hanging;
+ *                   gives up after the wait limit (2 s unless set below) and
+ *                   records device error 2 (tm_device_error) instead of hanging;
  *   tm_peer_exchange  tm_peer_signal then tm_peer_wait in one kernel launch
- *                   (flags = this rank's own flag buffer).
+ *                   (flags = this rank's own flag buffer);
+ *   tm_peer_set_wait_limit  limit, in ns, of the waits launched after the
+ *                   call (<= 0: back to the 2 s default); returns the old
+ *                   limit.  A wait that runs out advances its epoch counter
+ *                   like one that succeeded, so the next wait of that slot
+ *                   waits for the following epoch.
  * At most 8 ranks.  Plain peer stores and loads; no multicast.
  */
 TM_API int tm_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle);
@@ -142,6 +148,7 @@ TM_API int tm_peer_signal(void* const* peer_flags, int n_ranks, int rank, void* 
 TM_API int tm_peer_wait(const void* flags, int n_ranks, void* counters, int slot, void* stream);
 TM_API int tm_peer_exchange(void* const* peer_flags, int n_ranks, int rank, const void* flags,
                      void* counters, int slot, void* stream);
+TM_API int64_t tm_peer_set_wait_limit(int64_t ns);
 
 /*
  * A6/A11/A12. Row-span copies for the KV slot arena: commit-time append of a
@@ -315,8 +322,9 @@ TM_API int tm_attention_fwd_dev_tiles(const void* q, int64_t q_batch_stride, int
  * allowed.  The caller still passes q, K/V and out; the key-range split's
  * scratch is a fixed 16 MiB array in the library's own device memory, which
  * every GPU that loads the library keeps until the process exits.  Shapes
- * whose split needs more (tm_attention_workspace_bytes > 16 MiB) are
- * rejected with TM_ERR_INVALID_ARGUMENT.
+ * whose split needs more are rejected with TM_ERR_INVALID_ARGUMENT before
+ * anything is launched (the need is that of the partition the launch would
+ * choose; for one span it equals tm_attention_workspace_bytes).
  *   - The first call on a device looks up the array's device address (with
  *     that device current); make that first call before any stream capture.
  *   - All calls share the one array: calls that overlap on the GPU (other

@@ -114,6 +114,7 @@ _SIGS = {
     "tm_peer_wait": (ctypes.c_int, [c_vp, ctypes.c_int, c_vp, ctypes.c_int, c_vp]),
     "tm_peer_exchange": (ctypes.c_int, [ctypes.POINTER(c_vp), ctypes.c_int, ctypes.c_int, c_vp,
                                         c_vp, ctypes.c_int, c_vp]),
+    "tm_peer_set_wait_limit": (c_i64, [c_i64]),
     "tm_attention_fwd_noalloc": (ctypes.c_int, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64,
                                                 c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
                                                 ctypes.POINTER(KVSpan), ctypes.c_int, c_vp,

@@ -1111,15 +1111,23 @@ extern "C" int tm_attention_fwd_noalloc(const void* q, int64_t q_batch_stride,
   using namespace tmb::attn;
   if (!spans || n_spans < 1)
     return set_error(TM_ERR_INVALID_ARGUMENT, "attention: null pointer or no spans");
-  int64_t keys = 0;
-  for (int i = 0; i < n_spans; ++i)
-    if (spans[i].rows > 0) keys += spans[i].rows;
-  const int64_t need = tm_attention_workspace_bytes(B, Lq, H, D, keys);
+  if (D != 64 && D != 128) return set_error(TM_ERR_UNSUPPORTED, "attention: head dim %d", D);
+  if (B < 1 || Lq < 1 || H < 1)
+    return set_error(TM_ERR_INVALID_ARGUMENT, "attention: B=%d Lq=%d H=%d", B, Lq, H);
+  // The scratch need of the work partition the launch will choose: planned
+  // from the same key-tile list (each span starts a new tile) with no cap.
+  int2 tiles[kMaxTiles];
+  bool use_src[2] = {false, false};
+  int nt = 0;
+  const int st_tiles = build_tiles(spans, n_spans, cache_rows, new_rows, tiles, &nt, use_src);
+  if (st_tiles) return st_tiles;
+  const int64_t need =
+      split_ws_bytes(make_plan(B, Lq, H, D, nt, INT64_MAX).kv_splits, B, Lq, H, D);
   if (need > kNoAllocScratchBytes)
     return set_error(TM_ERR_INVALID_ARGUMENT,
-                     "attention (no-alloc): B=%d Lq=%d H=%d D=%d over %lld keys needs %lld bytes "
-                     "of scratch, above the fixed %lld bytes; use tm_attention_fwd_ws",
-                     B, Lq, H, D, (long long)keys, (long long)need,
+                     "attention (no-alloc): B=%d Lq=%d H=%d D=%d over %d key tiles needs %lld "
+                     "bytes of scratch, above the fixed %lld bytes; use tm_attention_fwd_ws",
+                     B, Lq, H, D, nt, (long long)need,
                      (long long)kNoAllocScratchBytes);
   void* scratch = nullptr;
   const int st = noalloc_scratch(&scratch);

@@ -25,10 +25,21 @@ int check_cuda(cudaError_t e, const char* what) {
   return set_error(TM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
+// The flag's device address, looked up once per device (with that device
+// current) and cached: the first launch on a device does the lookup, so that
+// first launch must come before any stream capture on that device.
 int* device_error_flag() {
-  void* p = nullptr;
-  if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
-  return static_cast<int*>(p);
+  static std::mutex mu;
+  static int* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
 }
 
 EncodeTiledFn encode_tiled() {

@@ -17,7 +17,8 @@ namespace tmb {
 int set_error(int status, const char* fmt, ...);
 int check_cuda(cudaError_t e, const char* what);
 
-// Device error flag (one int per device image of the library).
+// Device error flag (one int per device image of the library); its address
+// is cached per device after the first call on that device.
 int* device_error_flag();
 
 // cuTensorMapEncodeTiled, resolved once.

@@ -17,6 +17,7 @@
 //
 // Reference counterpart: the all_to_all_single calls of _seq_to_head /
 // _head_to_seq (taomate/runtime_support/parallel/all_to_all.py:125-173).
+#include <atomic>
 #include <cstring>
 
 #include "common.cuh"
@@ -27,8 +28,12 @@ namespace peer {
 
 constexpr int kMaxRanks = 8;
 constexpr int kSlots = 4;
-constexpr unsigned long long kPeerWaitNs = 2000000000ull;
+constexpr unsigned long long kPeerWaitNs = 2000000000ull;  // default limit of a wait
 constexpr int kDevPeerTimeout = 2;
+
+// Limit of the flag waits launched from now on (a kernel parameter, so a
+// captured graph keeps the limit it was captured with).
+std::atomic<unsigned long long> g_wait_limit_ns{kPeerWaitNs};
 
 // Flag array of a rank: int64 flags[kSlots][kMaxRanks], then the local
 // counters: sent[kSlots], awaited[kSlots].
@@ -55,7 +60,7 @@ __global__ void signal_kernel(const __grid_constant__ SignalParams p) {
 // Thread 0 waits until every rank's flag of `slot` reached this rank's next
 // awaited epoch (bounded; device error kDevPeerTimeout on giving up).
 __device__ void wait_flags(const unsigned long long* flags, unsigned long long* counters,
-                           int n_ranks, int slot, int* err) {
+                           int n_ranks, int slot, unsigned long long limit_ns, int* err) {
   const unsigned long long target = ++counters[kSlots + slot];
   const unsigned long long* f = flags + slot * kMaxRanks;
   const unsigned long long t0 = globaltimer_ns();
@@ -64,7 +69,7 @@ __device__ void wait_flags(const unsigned long long* flags, unsigned long long* 
       unsigned long long v;
       asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f + g) : "memory");
       if (v >= target) break;
-      if ((i & 63u) == 0u && globaltimer_ns() - t0 > kPeerWaitNs) {
+      if ((i & 63u) == 0u && globaltimer_ns() - t0 > limit_ns) {
         atomicCAS(err, 0, kDevPeerTimeout);
         return;
       }
@@ -74,14 +79,15 @@ __device__ void wait_flags(const unsigned long long* flags, unsigned long long* 
 }
 
 __global__ void wait_kernel(const unsigned long long* flags, unsigned long long* counters,
-                            int n_ranks, int slot, int* err) {
-  if (threadIdx.x == 0) wait_flags(flags, counters, n_ranks, slot, err);
+                            int n_ranks, int slot, unsigned long long limit_ns, int* err) {
+  if (threadIdx.x == 0) wait_flags(flags, counters, n_ranks, slot, limit_ns, err);
 }
 
 // signal_kernel then wait_kernel in one launch: a replayed graph pays one
 // node instead of two per exchange.
 __global__ void exchange_kernel(const __grid_constant__ SignalParams p,
-                                const unsigned long long* flags, int* err) {
+                                const unsigned long long* flags, unsigned long long limit_ns,
+                                int* err) {
   __shared__ unsigned long long epoch;
   if (threadIdx.x == 0) {
     epoch = ++p.counters[p.slot];
@@ -93,7 +99,7 @@ __global__ void exchange_kernel(const __grid_constant__ SignalParams p,
     unsigned long long* f = p.peer_flags[g] + p.slot * kMaxRanks + p.rank;
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(epoch) : "memory");
   }
-  if (threadIdx.x == 0) wait_flags(flags, p.counters, p.n_ranks, p.slot, err);
+  if (threadIdx.x == 0) wait_flags(flags, p.counters, p.n_ranks, p.slot, limit_ns, err);
 }
 
 }  // namespace peer
@@ -168,7 +174,7 @@ extern "C" int tm_peer_wait(const void* flags, int n_ranks, void* counters, int 
   if (!err) return set_error(TM_ERR_CUDA, "peer_wait: device error flag unavailable");
   wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const unsigned long long*>(flags), static_cast<unsigned long long*>(counters),
-      n_ranks, slot, err);
+      n_ranks, slot, g_wait_limit_ns.load(), err);
   return check_cuda(cudaGetLastError(), "peer_wait: launch");
 }
 
@@ -191,11 +197,17 @@ extern "C" int tm_peer_exchange(void* const* peer_flags, int n_ranks, int rank, 
   p.rank = rank;
   p.slot = slot;
   exchange_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      p, static_cast<const unsigned long long*>(flags), err);
+      p, static_cast<const unsigned long long*>(flags), g_wait_limit_ns.load(), err);
   return check_cuda(cudaGetLastError(), "peer_exchange: launch");
 }
 
 extern "C" int64_t tm_peer_flag_bytes(void) {
   using namespace tmb::peer;
   return static_cast<int64_t>(sizeof(unsigned long long)) * (kSlots * kMaxRanks + 2 * kSlots);
+}
+
+extern "C" int64_t tm_peer_set_wait_limit(int64_t ns) {
+  using namespace tmb::peer;
+  if (ns <= 0) ns = static_cast<int64_t>(kPeerWaitNs);
+  return static_cast<int64_t>(g_wait_limit_ns.exchange(static_cast<unsigned long long>(ns)));
 }

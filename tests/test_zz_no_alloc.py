@@ -10,8 +10,12 @@ caller allocates.
 Through the C ABI, two calls in a row (the second on different inputs, so
 anything stale in the shared array would show) are checked against the
 workspace entry point on the same inputs, at shapes whose work partition uses
-the scratch.  This file is collected last on purpose: if it fails, a run that
-stops at the first failure has already run every other test.
+the scratch.  Both entry points plan the same partition and launch the same
+kernels, so their outputs must be identical bit for bit.  Two more cases: a
+shape that needs no scratch (compared with tm_attention_fwd), and a shape whose
+partition needs more than the fixed array, which must be refused before
+anything is launched.  This file is collected last on purpose: if it fails, a
+run that stops at the first failure has already run every other test.
 """
 
 import ctypes
@@ -22,6 +26,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 DEV = torch.device("cuda", 0) if torch.cuda.is_available() else None
+FIXED_BYTES = 16 << 20
 
 SHAPES = [
     # (heads, dim_head, query rows, keys): 4 and 8 heads of the C2 chunk (the
@@ -47,19 +52,29 @@ def _args(lib_mod, q, k, v, out, H, D):
     return head, spans
 
 
+def _inputs(seed, H, D, Lq, Lk):
+    gen = torch.Generator().manual_seed(seed)
+    q = torch.randn(1, Lq, H, D, generator=gen).to(DEV, torch.bfloat16)
+    k = torch.randn(1, Lk, H, D, generator=gen).to(DEV, torch.bfloat16)
+    v = torch.randn(1, Lk, H, D, generator=gen).to(DEV, torch.bfloat16)
+    return q, k, v
+
+
+def _device_error_clear(lib):
+    code = ctypes.c_int(0)
+    assert lib.tm_device_error(ctypes.byref(code)) == 0 and code.value == 0
+
+
 @pytest.mark.parametrize("H,D,Lq,Lk", SHAPES)
 def test_noalloc_matches_workspace_entry_on_two_calls(H, D, Lq, Lk):
     from taomate_b200 import _lib
     lib = _lib.load()
     torch.cuda.set_device(DEV)
     need = lib.tm_attention_workspace_bytes(1, Lq, H, D, Lk)
-    assert 0 < need <= 16 << 20, "the shape must use the scratch and fit the fixed array"
+    assert 0 < need <= FIXED_BYTES, "the shape must use the scratch and fit the fixed array"
     stream = _lib.stream_ptr(DEV)
     for call in range(2):
-        gen = torch.Generator().manual_seed(1000 * call + H + D + Lq)
-        q = torch.randn(1, Lq, H, D, generator=gen).to(DEV, torch.bfloat16)
-        k = torch.randn(1, Lk, H, D, generator=gen).to(DEV, torch.bfloat16)
-        v = torch.randn(1, Lk, H, D, generator=gen).to(DEV, torch.bfloat16)
+        q, k, v = _inputs(1000 * call + H + D + Lq, H, D, Lq, Lk)
         out_na = torch.full_like(q, float("nan"))
         out_ws = torch.full_like(q, float("nan"))
         args, spans = _args(_lib, q, k, v, out_na, H, D)
@@ -71,12 +86,54 @@ def test_noalloc_matches_workspace_entry_on_two_calls(H, D, Lq, Lk):
         assert st == 0, lib.tm_last_error()
         torch.cuda.synchronize()
         assert torch.isfinite(out_na).all()
-        # the tests' bar between two runs of this kernel on the same inputs
-        assert _rel_l2(out_na, out_ws) < 4e-3
-        # and both against an fp32 reference, to the bf16 noise floor
+        # same partition, same kernels: identical bits
+        assert torch.equal(out_na, out_ws)
+        # and against an fp32 reference, to the bf16 noise floor
         ref = torch.nn.functional.scaled_dot_product_attention(
             q.transpose(1, 2).float(), k.transpose(1, 2).float(),
             v.transpose(1, 2).float()).transpose(1, 2)
         assert _rel_l2(out_na, ref) < 4e-3
-    code = ctypes.c_int(0)
-    assert lib.tm_device_error(ctypes.byref(code)) == 0 and code.value == 0
+    _device_error_clear(lib)
+
+
+def test_noalloc_without_split_equals_plain_entry():
+    """C2's 32 heads fill the GPU without a key-range split: the fixed array
+    goes unused and the result is the plain entry point's."""
+    from taomate_b200 import _lib
+    lib = _lib.load()
+    torch.cuda.set_device(DEV)
+    H, D, Lq, Lk = 32, 128, 1152, 4608
+    assert lib.tm_attention_workspace_bytes(1, Lq, H, D, Lk) == 0
+    stream = _lib.stream_ptr(DEV)
+    q, k, v = _inputs(7, H, D, Lq, Lk)
+    out_na = torch.full_like(q, float("nan"))
+    out_plain = torch.full_like(q, float("nan"))
+    args, spans = _args(_lib, q, k, v, out_na, H, D)
+    assert lib.tm_attention_fwd_noalloc(*args, stream) == 0, lib.tm_last_error()
+    args_p, spans_p = _args(_lib, q, k, v, out_plain, H, D)
+    assert lib.tm_attention_fwd(*args_p, stream) == 0, lib.tm_last_error()
+    torch.cuda.synchronize()
+    assert torch.equal(out_na, out_plain)
+    _device_error_clear(lib)
+
+
+def test_noalloc_refuses_shapes_above_the_fixed_array():
+    """23 heads of 44 queries over 4608 keys: the partition splits every
+    query tile into 32 key ranges, 16.06 MiB of partial outputs.  The call is
+    refused with TM_ERR_INVALID_ARGUMENT before any launch; out is untouched."""
+    from taomate_b200 import _lib
+    lib = _lib.load()
+    torch.cuda.set_device(DEV)
+    H, D, Lq, Lk = 23, 128, 44, 4608
+    need = lib.tm_attention_workspace_bytes(1, Lq, H, D, Lk)
+    assert need > FIXED_BYTES
+    q, k, v = _inputs(11, H, D, Lq, Lk)
+    out = torch.full_like(q, float("nan"))
+    args, spans = _args(_lib, q, k, v, out, H, D)
+    st = lib.tm_attention_fwd_noalloc(*args, _lib.stream_ptr(DEV))
+    assert st == _lib.TM_ERR_INVALID_ARGUMENT
+    msg = lib.tm_last_error().decode()
+    assert "tm_attention_fwd_ws" in msg and str(need) in msg
+    torch.cuda.synchronize()
+    assert torch.isnan(out.float()).all()
+    _device_error_clear(lib)
