@@ -183,6 +183,63 @@ TM_API int tm_strided_copy5(const void* src, void* dst, const int64_t* sizes,
                      void* stream);
 
 /*
+ * Block elementwise ops around the attention (f4): gated residual update,
+ * RMSNorm / LayerNorm and the AdaLN modulation in one pass over each token
+ * row.  Replaces, in block_forward_with_cache (ltx_causal/transformer/
+ * kv_cache.py:2145-2654):
+ *   rms_norm(x) * (1 + scale) + shift   (kv_cache.py:2200-2201, 2514-2525, 2604-2606)
+ *   x + out * gate                      (kv_cache.py:2217, 2566, 2579, 2610)
+ * with (shift, scale, gate) = table[i] + timestep[..., i, :] from
+ * CausalAVTransformerBlock.get_ada_values / get_av_ca_ada_values
+ * (ltx_causal/transformer/causal_block.py:434-478), and the LayerNorm +
+ * modulation of CausalLTXModel._process_output (causal_model.py:568-598).
+ *
+ * tm_ada_source: value of parameter p at column c for token row (b, t) =
+ *   table[p * D + c] + ts[b * ts_batch_stride + ((t + ts_row_offset) /
+ *   ts_row_div) * ts_row_stride + p * D + c]      (either pointer may be NULL).
+ * ts_row_div = tokens per frame reads per-frame parameter rows (the
+ * reference's per-token expansion, kv_cache.py:2970, is not needed); 1 reads
+ * per-token rows.
+ *
+ * tm_residual_norm, per row (b, t) of [B, L, D] bf16 tensors:
+ *   r = x + y * gate[gate_index]   (y NULL: r = x; gate NULL or index < 0: no gate)
+ *   x_out = r                      (when x_out is given; may alias x)
+ *   n = (r - mean) / sqrt(var + eps)  for norm_kind 1 (LayerNorm, no affine),
+ *       r / sqrt(mean(r^2) + eps)      for norm_kind 0 (RMSNorm, no weight),
+ *   outs[k] = n * (1 + scale) + shift (scale_index < 0: n), k < n_outs <= 2.
+ * fp32 arithmetic, one rounding per stored value; the norm reads the rounded
+ * residual.  D a multiple of 256, at most 8192; pointers 16-byte aligned,
+ * strides (elements) multiples of 8.
+ */
+typedef struct {
+  const void* table;
+  const void* ts;
+  int64_t ts_batch_stride, ts_row_stride;
+  int32_t ts_row_div, ts_row_offset;
+} tm_ada_source;
+
+typedef struct {
+  void* out;
+  int64_t batch_stride, row_stride;
+  tm_ada_source mod;
+  int32_t scale_index, shift_index;
+} tm_norm_output;
+
+TM_API int tm_residual_norm(const void* x, int64_t x_batch_stride, int64_t x_row_stride,
+                     const void* y, int64_t y_batch_stride, int64_t y_row_stride,
+                     const tm_ada_source* gate, int gate_index, void* x_out,
+                     int64_t x_out_batch_stride, int64_t x_out_row_stride,
+                     const tm_norm_output* outs, int n_outs, int norm_kind, int B, int L, int D,
+                     float eps, void* stream);
+
+/*
+ * In-place tanh-approximate GELU over n bf16 values (n a multiple of 8,
+ * 16-byte aligned): the activation of the FFN's first linear, GELUApprox
+ * (ltx_causal/transformer/compat.py:40, gelu(proj(x), approximate="tanh")).
+ */
+TM_API int tm_gelu_tanh(void* x, int64_t n, void* stream);
+
+/*
  * A7. Flash attention of a query chunk over a KV visibility list, on
  * tcgen05 tensor cores (TMA-fed tiles, fp32 accumulators in TMEM, online
  * softmax in registers).  Replaces the cache concat + SDPA of

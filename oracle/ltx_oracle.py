@@ -369,6 +369,122 @@ def cross_modal_pair_attention(a2v_params: Dict[str, np.ndarray], v2a_params: Di
 # ----------------------------------------------------------------------------
 # A4 / A8 / A13: Ulysses layout permutations (global view over all ranks)
 # ----------------------------------------------------------------------------
+# ----------------------------------------------------------------------------
+# f4: the transformer block around the attention
+# ----------------------------------------------------------------------------
+def attn_params(sd: Dict[str, np.ndarray], name: str) -> Dict[str, np.ndarray]:
+    """The ``to_q_w`` / ``q_norm_w`` ... parameter dict of attention module
+    ``name`` from a block state dict (``name.to_q.weight`` ...)."""
+    p = {}
+    for lin, key in (("to_q", "to_q"), ("to_k", "to_k"), ("to_v", "to_v"), ("to_out.0", "to_out"),
+                     ("to_gate_logits", "to_gate_logits")):
+        if f"{name}.{lin}.weight" in sd:
+            p[key + "_w"] = sd[f"{name}.{lin}.weight"]
+            p[key + "_b"] = sd[f"{name}.{lin}.bias"]
+    p["q_norm_w"] = sd[f"{name}.q_norm.weight"]
+    p["k_norm_w"] = sd[f"{name}.k_norm.weight"]
+    return p
+
+
+def ada_values(table: np.ndarray, ts: np.ndarray, idx: Sequence[int], dtype=np.float64):
+    """``table[i] + timestep[:, i]`` for i in ``idx`` (CausalAVTransformerBlock.
+    get_ada_values, ltx_causal/transformer/causal_block.py:434-452); ``ts`` is
+    ``[L, n * D]`` (one row per token) or ``[1, n * D]``."""
+    n, D = table.shape
+    t = np.asarray(ts, dtype=dtype).reshape(ts.shape[0], n, D)
+    return [np.asarray(table[i], dtype=dtype)[None] + t[:, i] for i in idx]
+
+
+def gelu_tanh(x: np.ndarray) -> np.ndarray:
+    """GELU, tanh approximation (GELUApprox, ltx_causal/transformer/compat.py:40)."""
+    return 0.5 * x * (1.0 + np.tanh(math.sqrt(2.0 / math.pi) * (x + 0.044715 * x ** 3)))
+
+
+def feed_forward(sd: Dict[str, np.ndarray], name: str, x: np.ndarray, dtype=np.float64):
+    """FeedForward (compat.py:47-70): Linear -> tanh GELU -> Linear."""
+    f = lambda a: np.asarray(a, dtype=dtype)
+    h = f(x) @ f(sd[f"{name}.net.0.proj.weight"]).T + f(sd[f"{name}.net.0.proj.bias"])
+    return gelu_tanh(h) @ f(sd[f"{name}.net.2.weight"]).T + f(sd[f"{name}.net.2.bias"])
+
+
+def block_forward_with_cache(sd: Dict[str, np.ndarray], cfg: Dict[str, int], vx: np.ndarray,
+                             ax: np.ndarray, video_ts: np.ndarray, audio_ts: np.ndarray,
+                             video_pe, audio_pe, video_cross_pe, audio_cross_pe,
+                             video_ctx: np.ndarray, audio_ctx: np.ndarray,
+                             video_mask: Optional[np.ndarray], audio_mask: Optional[np.ndarray],
+                             video_cross_ss: np.ndarray, video_cross_gate: np.ndarray,
+                             audio_cross_ss: np.ndarray, audio_cross_gate: np.ndarray,
+                             caches: Dict[str, Tuple[Optional[np.ndarray], Optional[np.ndarray]]],
+                             video_real_len: Optional[int] = None,
+                             audio_real_len: Optional[int] = None, eps: float = 1e-6,
+                             dtype=np.float64):
+    """One block with KV cache (block_forward_with_cache,
+    ltx_causal/transformer/kv_cache.py:2145-2654, the default path:
+    cross_attention_adaln off, no learned memory, A2V/V2A as two calls).
+
+    ``sd``: block state dict (reference names); ``cfg``: ``video_heads``,
+    ``video_dim_head``, ``audio_heads``, ``audio_dim_head``.  Activations
+    ``[L, D]``; AdaLN rows per token (``video_ts [Lv, 6 Dv]``, ``*_cross_ss
+    [L, 4 D]``, ``*_cross_gate [L, D]``); masks ``[Lk]`` 0/1 or None; ``caches``
+    maps ``video_self`` / ``audio_self`` / ``a2v`` / ``v2a`` to ``(k, v)``
+    ``[L, H, D]`` or ``(None, None)``.  Returns ``(vx, ax, new)`` with ``new``
+    the same map holding this call's new K/V rows.
+    Order (kv_cache.py:2197-2640): video self (:2197-2218), video text cross
+    (:2441-2460), audio self (:2464-2490), audio text cross (:2493-2510),
+    norm3 + A2V + V2A (:2512-2598, get_av_ca_ada_values causal_block.py:454-478),
+    video FFN (:2600-2618), audio FFN (:2620-2640).
+    """
+    f = lambda a: np.asarray(a, dtype=dtype)
+    Hv, dv = cfg["video_heads"], cfg["video_dim_head"]
+    Ha, da = cfg["audio_heads"], cfg["audio_dim_head"]
+    rms = lambda x: rms_norm(x, None, eps)
+    vx, ax = f(vx), f(ax)
+    new = {}
+    tab = lambda k: f(sd[k])
+    sh, sc, g = ada_values(tab("scale_shift_table"), video_ts, (0, 1, 2), dtype)
+    out, k, v = attention_with_cache(rms(vx) * (1 + sc) + sh, attn_params(sd, "attn1"), Hv, dv,
+                                     video_pe, *caches["video_self"],
+                                     new_kv_real_len=video_real_len, eps=eps, dtype=dtype)
+    new["video_self"] = (k, v)
+    vx = vx + out * g
+    vm = None if video_mask is None else video_mask[None]
+    vx = vx + text_cross_attention(rms(vx)[None], f(video_ctx)[None], attn_params(sd, "attn2"),
+                                   Hv, dv, mask=vm, eps=eps, dtype=dtype)[0]
+    sh, sc, g = ada_values(tab("audio_scale_shift_table"), audio_ts, (0, 1, 2), dtype)
+    out, k, v = attention_with_cache(rms(ax) * (1 + sc) + sh, attn_params(sd, "audio_attn1"), Ha,
+                                     da, audio_pe, *caches["audio_self"],
+                                     new_kv_real_len=audio_real_len, eps=eps, dtype=dtype)
+    new["audio_self"] = (k, v)
+    ax = ax + out * g
+    am = None if audio_mask is None else audio_mask[None]
+    ax = ax + text_cross_attention(rms(ax)[None], f(audio_ctx)[None],
+                                   attn_params(sd, "audio_attn2"), Ha, da, mask=am, eps=eps,
+                                   dtype=dtype)[0]
+    vn, an = rms(vx), rms(ax)
+    tv, ta = tab("scale_shift_table_a2v_ca_video"), tab("scale_shift_table_a2v_ca_audio")
+    sc_va, sh_va, sc_vv, sh_vv = ada_values(tv[:4], video_cross_ss, (0, 1, 2, 3), dtype)
+    (g_a2v,) = ada_values(tv[4:], video_cross_gate, (0,), dtype)
+    sc_aa, sh_aa, sc_av, sh_av = ada_values(ta[:4], audio_cross_ss, (0, 1, 2, 3), dtype)
+    (g_v2a,) = ada_values(ta[4:], audio_cross_gate, (0,), dtype)
+    a2v, k, v = attention_with_cache(vn * (1 + sc_va) + sh_va, attn_params(sd, "audio_to_video_attn"),
+                                     Ha, da, video_cross_pe, *caches["a2v"],
+                                     context=an * (1 + sc_aa) + sh_aa, k_pe=audio_cross_pe,
+                                     new_kv_real_len=audio_real_len, eps=eps, dtype=dtype)
+    new["a2v"] = (k, v)
+    v2a, k, v = attention_with_cache(an * (1 + sc_av) + sh_av, attn_params(sd, "video_to_audio_attn"),
+                                     Ha, da, audio_cross_pe, *caches["v2a"],
+                                     context=vn * (1 + sc_vv) + sh_vv, k_pe=video_cross_pe,
+                                     new_kv_real_len=video_real_len, eps=eps, dtype=dtype)
+    new["v2a"] = (k, v)
+    vx = vx + a2v * g_a2v
+    ax = ax + v2a * g_v2a
+    sh, sc, g = ada_values(tab("scale_shift_table"), video_ts, (3, 4, 5), dtype)
+    vx = vx + feed_forward(sd, "ff", rms(vx) * (1 + sc) + sh, dtype) * g
+    sh, sc, g = ada_values(tab("audio_scale_shift_table"), audio_ts, (3, 4, 5), dtype)
+    ax = ax + feed_forward(sd, "audio_ff", rms(ax) * (1 + sc) + sh, dtype) * g
+    return vx, ax, new
+
+
 def seq_to_head(shards: List[np.ndarray]) -> List[np.ndarray]:
     """Seq-sharded ``[B, S/G, H, D]`` per rank -> head-sharded ``[B, S, H/G, D]``.
 

@@ -5,6 +5,7 @@ Modules mirror the reference's layout for this path:
   rope       -> ltx_causal/rope/causal_rope.py
   attention  -> ltx_causal/transformer/kv_cache.py (attention_with_cache)
                 ltx_causal/attention/flex_attention_utils.py (standard_attention_forward)
+  block      -> ltx_causal/transformer/kv_cache.py (block_forward_with_cache)
   kv_cache   -> LayerKVCache / KVCache / _cat_cache, plus the slot arena
   cache      -> taomate/inference/cache.py (segments, retain_streaming_context)
   parallel   -> taomate/runtime_support/parallel (Ulysses SP)
@@ -19,6 +20,8 @@ from .attention import (_cross_modal_pair_attention_with_cache, attention_with_c
 from .kv_cache import (ArenaKV, ArenaSpec, KVArena, KVCache, LayerKVCache, _cat_cache,
                        cat_cache_pair, init_arena_cache)
 from .cache import (attach_segments, cache_segments, retain_streaming_context, retain_window)
+from . import block
+from .block import BlockWeights, block_forward_with_cache, fuse_block_weights
 
 __all__ = [
     "CausalRopeType", "apply_split_rotary_emb", "causal_precompute_freqs_cis",
@@ -28,4 +31,5 @@ __all__ = [
     "ArenaKV", "ArenaSpec", "KVArena", "KVCache", "LayerKVCache", "_cat_cache",
     "cat_cache_pair", "init_arena_cache",
     "attach_segments", "cache_segments", "retain_streaming_context", "retain_window",
+    "block", "BlockWeights", "block_forward_with_cache", "fuse_block_weights",
 ]

@@ -60,6 +60,18 @@ class KVSpan(ctypes.Structure):
                 ("rows", ctypes.c_int32)]
 
 
+class AdaSource(ctypes.Structure):
+    _fields_ = [("table", c_vp), ("ts", c_vp), ("ts_batch_stride", c_i64),
+                ("ts_row_stride", c_i64), ("ts_row_div", ctypes.c_int32),
+                ("ts_row_offset", ctypes.c_int32)]
+
+
+class NormOutput(ctypes.Structure):
+    _fields_ = [("out", c_vp), ("batch_stride", c_i64), ("row_stride", c_i64),
+                ("mod", AdaSource), ("scale_index", ctypes.c_int32),
+                ("shift_index", ctypes.c_int32)]
+
+
 # name -> (restype, argtypes)
 _SIGS = {
     "tm_abi_version": (ctypes.c_int, []),
@@ -115,6 +127,12 @@ _SIGS = {
     "tm_peer_exchange": (ctypes.c_int, [ctypes.POINTER(c_vp), ctypes.c_int, ctypes.c_int, c_vp,
                                         c_vp, ctypes.c_int, c_vp]),
     "tm_peer_set_wait_limit": (c_i64, [c_i64]),
+    "tm_residual_norm": (ctypes.c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64,
+                                        ctypes.POINTER(AdaSource), ctypes.c_int, c_vp, c_i64,
+                                        c_i64, ctypes.POINTER(NormOutput), ctypes.c_int,
+                                        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_float, c_vp]),
+    "tm_gelu_tanh": (ctypes.c_int, [c_vp, c_i64, c_vp]),
     "tm_attention_fwd_noalloc": (ctypes.c_int, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64,
                                                 c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
                                                 ctypes.POINTER(KVSpan), ctypes.c_int, c_vp,

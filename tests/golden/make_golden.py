@@ -21,14 +21,17 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("TAOMATE_REFERENCE", "/root/reference")
+REF = os.environ.get("TAOMATE_REFERENCE")
 sys.path.insert(0, HERE)
 import inputs  # noqa: E402
 
 
 def _import_reference():
+    if not REF:
+        raise SystemExit("set TAOMATE_REFERENCE to the TaoMate source tree (the directory that "
+                         "holds ltx_causal/ and taomate/)")
     if not os.path.isdir(REF):
-        raise SystemExit(f"reference tree not found at {REF}")
+        raise SystemExit(f"reference tree not found at TAOMATE_REFERENCE={REF}")
     sys.path.insert(0, REF)
     import torch  # noqa: F401
     from ltx_causal.rope import causal_rope
@@ -220,6 +223,171 @@ def gen_pair(causal_rope, CausalLTXAttention, kv_cache, torch):
         np.savez_compressed(os.path.join(HERE, f"pair_{name}.npz"), **rec)
 
 
+def _bf16_bits(t):
+    """bf16 tensor -> its raw 16-bit patterns (exact, half the bytes of f32)."""
+    return t.detach().to("cpu").contiguous().view(torch_int16()).numpy().view(np.uint16)
+
+
+def torch_int16():
+    import torch
+    return torch.int16
+
+
+def _sampled(rec, key, t, rows):
+    """Store rows ``rows`` of a [1, L, ...] output: fp32 as float32, bf16 as bits."""
+    import torch
+    r = torch.from_numpy(rows)
+    sub = t[0].index_select(0, r)
+    if t.dtype == torch.bfloat16:
+        rec[key] = _bf16_bits(sub)
+    else:
+        rec[key] = f32(sub)
+
+
+def gen_full(causal_rope, CausalLTXAttention, kv_cache, torch):
+    """The full-size cases (BASELINE configs 2 and 3): attention_with_cache
+    and the paired cross-modal attention at their real shapes, on inputs
+    already rounded to bf16, in fp32 (the exact answer for those inputs) and
+    in bf16 (the reference's deployed precision).  Sampled rows only."""
+    for name in inputs.FULL_ATTN_CASES:
+        d = inputs.attn_case_inputs(name)
+        c, prm = d["cfg"], d["params"]
+        heads, dh, hid = c["heads"], c["dim_head"], c["hidden"]
+        attn = CausalLTXAttention(hid, None, heads=heads, dim_head=dh,
+                                  apply_gated_attention=c["gated"])
+        _load_module(attn, prm, torch)
+        x = torch.from_numpy(d["x"])[None]
+        ck = torch.from_numpy(d["cached_k"])[None]
+        cv = torch.from_numpy(d["cached_v"])[None]
+        g = torch.tensor([list(c["grid"])])
+        cos, sin = causal_rope.causal_precompute_freqs_cis(
+            g, heads * dh, start_frame=c["start"], device="cpu", num_attention_heads=heads,
+            is_audio=c["audio"], max_pos=[20] if len(c["grid"]) == 1 else None)
+        rows_out = inputs.full_rows(c["lq"])
+        rows_kv = inputs.full_rows(c["lq"], 48)
+        rec = {"rows_out": rows_out, "rows_kv": rows_kv}
+        for tag, dt in (("f32", torch.float32), ("bf16", torch.bfloat16)):
+            a = attn.to(dt)
+            with torch.no_grad():
+                out, nk, nv = kv_cache.attention_with_cache(
+                    a, x.to(dt), None, (cos.to(dt), sin.to(dt)), None, ck.to(dt), cv.to(dt),
+                    new_kv_real_len=c["real_len"])
+            _sampled(rec, f"out_{tag}", out, rows_out)
+            _sampled(rec, f"new_k_{tag}", nk, rows_kv)
+            _sampled(rec, f"new_v_{tag}", nv, rows_kv)
+        np.savez_compressed(os.path.join(HERE, f"full_attn_{name}.npz"), **rec)
+        print("full", name, flush=True)
+    for name in inputs.FULL_PAIR_CASES:
+        d = inputs.pair_case_inputs(name)
+        c = d["cfg"]
+        H, D = c["heads"], c["dim_head"]
+        inner = H * D
+        a2v = CausalLTXAttention(c["v_hidden"], c["a_hidden"], heads=H, dim_head=D,
+                                 apply_gated_attention=c["gated"][0])
+        v2a = CausalLTXAttention(c["a_hidden"], c["v_hidden"], heads=H, dim_head=D,
+                                 apply_gated_attention=c["gated"][1])
+        _load_module(a2v, d["a2v"], torch)
+        _load_module(v2a, d["v2a"], torch)
+        vc, vs = causal_rope.causal_precompute_freqs_cis(
+            torch.tensor([[c["v_frames"]]]), inner, max_pos=[20], start_frame=c["v_start"],
+            device="cpu", is_audio=False, num_attention_heads=H)
+        fs = c["frame_seqlen"]
+        expand = lambda t: t.unsqueeze(3).expand(-1, -1, -1, fs, -1).reshape(
+            t.shape[0], t.shape[1], t.shape[2] * fs, t.shape[3])
+        vc, vs = expand(vc), expand(vs)
+        ac, as_ = causal_rope.causal_precompute_freqs_cis(
+            torch.tensor([[c["la"]]]), inner, max_pos=[20], start_frame=c["a_start"],
+            device="cpu", is_audio=True, num_attention_heads=H)
+        lv = d["lv"]
+        rows = {"a2v_out": inputs.full_rows(lv), "a2v_k": inputs.full_rows(c["la"]),
+                "a2v_v": inputs.full_rows(c["la"]), "v2a_out": inputs.full_rows(c["la"]),
+                "v2a_k": inputs.full_rows(lv, 48), "v2a_v": inputs.full_rows(lv, 48)}
+        rec = {f"rows_{k}": v for k, v in rows.items()}
+        for tag, dt in (("f32", torch.float32), ("bf16", torch.bfloat16)):
+            t = lambda a: None if a is None else torch.from_numpy(a)[None].to(dt)
+            cache = kv_cache.LayerKVCache()
+            for nm in ("a2v", "v2a"):
+                kv = d["caches"][nm]
+                if kv is not None:
+                    setattr(cache, nm + "_k", t(kv[0]))
+                    setattr(cache, nm + "_v", t(kv[1]))
+            with torch.no_grad():
+                outs = kv_cache._cross_modal_pair_attention_with_cache(
+                    a2v.to(dt), v2a.to(dt), t(d["x"]["vx_a2v"]), t(d["x"]["ax_a2v"]),
+                    t(d["x"]["ax_v2a"]), t(d["x"]["vx_v2a"]), (vc.to(dt), vs.to(dt)),
+                    (ac.to(dt), as_.to(dt)), cache, video_real_len=c["video_real_len"],
+                    audio_real_len=c["audio_real_len"], layer_idx=0)
+            for key, o in zip(("a2v_out", "a2v_k", "a2v_v", "v2a_out", "v2a_k", "v2a_v"), outs):
+                _sampled(rec, f"{key}_{tag}", o, rows[key])
+        np.savez_compressed(os.path.join(HERE, f"full_pair_{name}.npz"), **rec)
+        print("full pair", name, flush=True)
+
+
+def gen_block(causal_rope, kv_cache, torch):
+    """block_forward_with_cache (kv_cache.py:2145-2654) of a real reference
+    CausalAVTransformerBlock loaded with the seeded weights (strict state
+    dict), fp32 and bf16, with the text K/V cache off (the reference default)
+    and the PE tables / per-token AdaLN rows built as model_forward_inference
+    builds them (kv_cache.py:2906-3000, 2960-2970)."""
+    from ltx_causal.transformer.causal_block import CausalAVTransformerBlock, TransformerConfig
+    kv_cache._CACHE_TEXT_CROSS_KV = False
+    for name in inputs.BLOCK_CASES:
+        d = inputs.block_case_inputs(name)
+        c = d["cfg"]
+        Dv, Da = c["video_dim"], c["audio_dim"]
+        Hv, dv, Ha, da = c["video_heads"], c["video_dim_head"], c["audio_heads"], c["audio_dim_head"]
+        blk = CausalAVTransformerBlock(
+            0, video=TransformerConfig(dim=Dv, heads=Hv, d_head=dv, context_dim=Dv),
+            audio=TransformerConfig(dim=Da, heads=Ha, d_head=da, context_dim=Da))
+        blk.load_state_dict({k: torch.from_numpy(v) for k, v in d["params"].items()}, strict=True)
+        blk.eval()
+        F, fs, La, Lv = c["v_frames"], c["fh"] * c["fw"], c["la"], d["Lv"]
+        vpe = causal_rope.causal_precompute_freqs_cis(
+            torch.tensor([[F, c["fh"], c["fw"]]]), Hv * dv, start_frame=c["v_start"],
+            device="cpu", num_attention_heads=Hv)
+        ape = causal_rope.causal_precompute_freqs_cis(
+            torch.tensor([[La]]), Ha * da, max_pos=[20], start_frame=c["a_start"], device="cpu",
+            is_audio=True, num_attention_heads=Ha)
+        vc, vs = causal_rope.causal_precompute_freqs_cis(
+            torch.tensor([[F]]), Ha * da, max_pos=[20], start_frame=c["v_start"], device="cpu",
+            is_audio=False, num_attention_heads=Ha)
+        expand = lambda t: t.unsqueeze(3).expand(-1, -1, -1, fs, -1).reshape(
+            t.shape[0], t.shape[1], t.shape[2] * fs, t.shape[3])
+        vcpe = (expand(vc), expand(vs))
+        acpe = causal_rope.causal_precompute_freqs_cis(
+            torch.tensor([[La]]), Ha * da, max_pos=[20], start_frame=c["a_start"], device="cpu",
+            is_audio=True, num_attention_heads=Ha)
+        x = {k: torch.from_numpy(v)[None] for k, v in d["x"].items()}
+        per_tok = lambda t: t.repeat_interleave(fs, dim=1)  # per-frame rows -> per token
+        rec = {}
+        for tag, dt in (("f32", torch.float32), ("bf16", torch.bfloat16)):
+            b = blk.to(dt)
+            cv = lambda t: t.to(dt)
+            m = torch.from_numpy(d["mask"])[None]
+            mask = (m - 1).to(dt).reshape(1, 1, 1, -1) * torch.finfo(dt).max
+            lc = kv_cache.LayerKVCache(**{
+                f"{nm}_{kv}": torch.from_numpy(arr)[None].to(dt)
+                for nm, pair in d["caches"].items() for kv, arr in zip("kv", pair)})
+            with torch.no_grad():
+                vx, ax, new = kv_cache.block_forward_with_cache(
+                    b, cv(x["video_x"]), cv(x["audio_x"]), cv(per_tok(x["video_ts"])),
+                    cv(x["audio_ts"]), tuple(map(cv, vpe)), tuple(map(cv, ape)),
+                    tuple(map(cv, vcpe)), tuple(map(cv, acpe)), cv(x["video_ctx"]),
+                    cv(x["audio_ctx"]), mask, mask, cv(per_tok(x["video_cross_ss"])),
+                    cv(per_tok(x["video_cross_gate"])), cv(x["audio_cross_ss"]),
+                    cv(x["audio_cross_gate"]), None, None, None, None, lc, layer_idx=0,
+                    video_frame_seqlen=fs, audio_frame_seqlen=1)
+            rec[f"video_x_{tag}"] = f32(vx[0])
+            rec[f"audio_x_{tag}"] = f32(ax[0])
+            for fld, n_new in (("video_self_k", Lv), ("video_self_v", Lv), ("audio_self_k", La),
+                               ("audio_self_v", La), ("a2v_k", La), ("a2v_v", La),
+                               ("v2a_k", Lv), ("v2a_v", Lv)):
+                t = getattr(new, fld)
+                rec[f"{fld}_{tag}"] = f32(t[0, -n_new:])
+        np.savez_compressed(os.path.join(HERE, f"block_{name}.npz"), **rec)
+        print("block", name, flush=True)
+
+
 def gen_attention(causal_rope, CausalLTXAttention, kv_cache, torch):
     for name in inputs.ATTN_CASES:
         _attn_case(causal_rope, CausalLTXAttention, kv_cache, torch, name)
@@ -340,6 +508,8 @@ def main():
         "pair": lambda: gen_pair(causal_rope, CausalLTXAttention, kv_cache, torch),
         "cache": lambda: gen_cache(kv_cache, tcache, torch, compute_av_blocks),
         "a2a": gen_a2a,
+        "full": lambda: gen_full(causal_rope, CausalLTXAttention, kv_cache, torch),
+        "block": lambda: gen_block(causal_rope, kv_cache, torch),
     }
     for name in (sys.argv[1:] or list(groups)):  # e.g. `make_golden.py pair`
         groups[name]()

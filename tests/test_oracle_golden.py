@@ -128,6 +128,94 @@ def test_cross_modal_pair_matches_reference(golden_dir, case):
         assert rel_l2(g, z[f"{key}_bf16"]) < 2e-2, key
 
 
+def _bits_to_f32(b):
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+@pytest.mark.parametrize("case", ["c2", "c3_audio"])
+def test_attention_with_cache_full_size_matches_reference(golden_dir, case):
+    """The restatement at BASELINE config 2 / 3 shapes against the reference's
+    fp32 run on the same bf16-rounded inputs (sampled rows).  The oracle
+    builds its own RoPE tables, so fp32 table ulps enter at ~1e-6."""
+    z = _load(golden_dir, f"full_attn_{case}.npz")
+    d = inputs.attn_case_inputs(case)
+    c = d["cfg"]
+    cos, sin = O.precompute_freqs_cis_split(c["grid"], c["heads"] * c["dim_head"],
+                                            start_frame=c["start"], is_audio=c["audio"],
+                                            num_heads=c["heads"], precision="f32",
+                                            max_pos=[20] if len(c["grid"]) == 1 else None)
+    out, nk, nv = O.attention_with_cache(d["x"], d["params"], c["heads"], c["dim_head"],
+                                         (cos, sin), d["cached_k"], d["cached_v"],
+                                         new_kv_real_len=c["real_len"])
+    ro, rk = z["rows_out"], z["rows_kv"]
+    assert rel_l2(out[ro], z["out_f32"]) < 1e-4
+    assert rel_l2(nk[rk], z["new_k_f32"]) < 1e-4
+    assert rel_l2(nv[rk], z["new_v_f32"]) < 1e-4
+    # the reference's own bf16 run on the same inputs, for scale
+    assert rel_l2(out[ro], _bits_to_f32(z["out_bf16"])) < 1e-2
+
+
+def test_cross_modal_pair_full_size_matches_reference(golden_dir):
+    z = _load(golden_dir, "full_pair_c3.npz")
+    d = inputs.pair_case_inputs("c3")
+    c = d["cfg"]
+    inner = c["heads"] * c["dim_head"]
+    vc, vs = O.precompute_freqs_cis_split((c["v_frames"],), inner, start_frame=c["v_start"],
+                                          num_heads=c["heads"], precision="f32", max_pos=[20])
+    vc = np.repeat(vc, c["frame_seqlen"], axis=1)
+    vs = np.repeat(vs, c["frame_seqlen"], axis=1)
+    ac, as_ = O.precompute_freqs_cis_split((c["la"],), inner, start_frame=c["a_start"],
+                                           is_audio=True, num_heads=c["heads"], precision="f32",
+                                           max_pos=[20])
+    got = O.cross_modal_pair_attention(
+        d["a2v"], d["v2a"], c["heads"], c["dim_head"], d["x"]["vx_a2v"], d["x"]["ax_a2v"],
+        d["x"]["ax_v2a"], d["x"]["vx_v2a"], (vc, vs), (ac, as_), d["caches"]["a2v"],
+        d["caches"]["v2a"], video_real_len=c["video_real_len"],
+        audio_real_len=c["audio_real_len"])
+    for key, g in zip(PAIR_KEYS, got):
+        rows = z[f"rows_{key}"]
+        assert rel_l2(g[rows], z[f"{key}_f32"]) < 1e-4, key
+
+
+BLOCK_NEW = (("video_self", "video_self_k", "video_self_v"), ("audio_self", "audio_self_k",
+              "audio_self_v"), ("a2v", "a2v_k", "a2v_v"), ("v2a", "v2a_k", "v2a_v"))
+
+
+def block_oracle_inputs(d):
+    """The oracle's arguments for a block golden case: PE tables as the model
+    forward builds them and per-token AdaLN rows."""
+    c, x, fs = d["cfg"], d["x"], d["frame_seqlen"]
+    Hv, dv, Ha, da = c["video_heads"], c["video_dim_head"], c["audio_heads"], c["audio_dim_head"]
+    F = c["v_frames"]
+    vpe = O.precompute_freqs_cis_split((F, c["fh"], c["fw"]), Hv * dv, start_frame=c["v_start"],
+                                       num_heads=Hv, precision="f32")
+    ape = O.precompute_freqs_cis_split((c["la"],), Ha * da, start_frame=c["a_start"],
+                                       is_audio=True, num_heads=Ha, precision="f32", max_pos=[20])
+    vc, vs = O.precompute_freqs_cis_split((F,), Ha * da, start_frame=c["v_start"], num_heads=Ha,
+                                          precision="f32", max_pos=[20])
+    vcpe = (np.repeat(vc, fs, axis=1), np.repeat(vs, fs, axis=1))
+    tok = lambda a: np.repeat(a, fs, axis=0)
+    return (x["video_x"], x["audio_x"], tok(x["video_ts"]), x["audio_ts"], vpe, ape, vcpe, ape,
+            x["video_ctx"], x["audio_ctx"], d["mask"], d["mask"], tok(x["video_cross_ss"]),
+            tok(x["video_cross_gate"]), x["audio_cross_ss"], x["audio_cross_gate"])
+
+
+def test_block_forward_matches_reference(golden_dir):
+    """The whole-block restatement against a real reference block (same
+    seeded weights loaded by state-dict name) run in fp32."""
+    z = _load(golden_dir, "block_small.npz")
+    d = inputs.block_case_inputs("small")
+    vx, ax, new = O.block_forward_with_cache(d["params"], d["cfg"], *block_oracle_inputs(d),
+                                             caches=d["caches"])
+    assert rel_l2(vx, z["video_x_f32"]) < 1e-4
+    assert rel_l2(ax, z["audio_x_f32"]) < 1e-4
+    for nm, kk, vk in BLOCK_NEW:
+        assert rel_l2(new[nm][0], z[f"{kk}_f32"]) < 1e-4, kk
+        assert rel_l2(new[nm][1], z[f"{vk}_f32"]) < 1e-4, vk
+    # the reference's own bf16 run, for scale
+    assert rel_l2(vx, z["video_x_bf16"]) < 1e-2
+
+
 def test_av_blocks_known_answers(golden_dir):
     with open(os.path.join(golden_dir, "av_blocks.json")) as fh:
         kab = json.load(fh)
