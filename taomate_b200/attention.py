@@ -269,14 +269,11 @@ def _text_kv(attn, context: Tensor, base_context: Tensor, prompt_cache_key, cach
                 cache.move_to_end(key)
                 return k, v
             cache.pop(key, None)
+    # all heads: every rank holds the whole text context, so under sequence
+    # parallelism it attends its own query tokens over all heads locally
     k = F.linear(context, attn.to_k.weight, attn.to_k.bias)
     (k,) = norm_rope([k], [attn.k_norm.weight], [None], H, D, _norm_eps(attn.k_norm))
     v = F.linear(context, attn.to_v.weight, attn.to_v.bias).view(B, -1, H, D)
-    if sp_size > 1:
-        Hl = H // sp_size
-        h0 = P.get_sp_rank() * Hl
-        k = k.narrow(2, h0, Hl).contiguous()
-        v = v.narrow(2, h0, Hl).contiguous()
     if key is not None:
         cache[key] = (weakref.ref(base_context), k, v)
         cache.move_to_end(key)
@@ -293,24 +290,24 @@ def text_cross_attention_with_kv_cache(attn, x: Tensor, context: Tensor, *,
     (``_text_cross_attention_with_kv_cache``, kv_cache.py:764-827): video
     queries against a prompt's text tokens; the padding mask becomes the
     kernel's key spans (no mask tensor is built), K/V projections are cached
-    per prompt as the reference does, Q goes through seq->head under SP and
-    the output back through head->seq, then gate and out projection."""
+    per prompt as the reference does, then gate and out projection.
+
+    Under sequence parallelism the reference moves Q seq->head, attends one
+    head group against head-narrowed K/V and moves the output head->seq
+    (kv_cache.py:797-817).  Every rank already holds the whole text context,
+    so here each rank attends its own query tokens over all heads: the same
+    values per (token, head), no exchange."""
     B = int(x.shape[0])
     H, D = int(attn.heads), int(attn.dim_head)
     sp_size = P.get_sp_world_size() if P.is_sp_enabled() else 1
     with section(f"{cache_name}.text_q_project"):
         q = F.linear(x, attn.to_q.weight, attn.to_q.bias)
         (q,) = norm_rope([q], [attn.q_norm.weight], [None], H, D, _norm_eps(attn.q_norm))
-        if sp_size > 1:
-            q = P.seq_all_to_all_head(q, P.get_sp_group(), sp_size)
     k, v = _text_kv(attn, context, base_context, prompt_cache_key, cache_name, sp_size)
     runs = [[(0, int(k.shape[1]))]] * B if mask is None else key_padding_runs(mask, B,
                                                                             int(k.shape[1]))
     with section(f"{cache_name}.text_sdpa"):
         out = _masked_attention(q, k, v, runs)
-    if sp_size > 1:
-        with section(f"{cache_name}.text_a2a_head2seq"):
-            out = P.head_all_to_all_seq(out, P.get_sp_group(), sp_size)
     out = out.reshape(B, -1, H * D)
     if getattr(attn, "to_gate_logits", None) is not None:
         gates = 2.0 * torch.sigmoid(attn.to_gate_logits(x))
@@ -460,7 +457,15 @@ def attention_with_cache(
     H, D = int(attn.heads), int(attn.dim_head)
     sp_size = P.get_sp_world_size() if P.is_sp_enabled() else 1
     if sp_size > 1 and not sp_context_sharded:
-        raise NotImplementedError("text cross-attention (replicated K/V) is not on this path")
+        # The context is replicated on every rank (text cross-attention): the
+        # reference narrows K/V to this rank's heads after a seq->head move of
+        # Q (kv_cache.py:1446-1451).  Attending this rank's query tokens over
+        # all heads gives the same values per (token, head) with no exchange;
+        # cached and returned K/V then hold all heads.
+        with P.sp_local():
+            return attention_with_cache(attn, x, context, pe, k_pe, cached_k, cached_v,
+                                        logit_log_scale, pyramid_policy, layer_idx, modality,
+                                        frame_seqlen, True, new_kv_real_len, profile_name)
 
     base = profile_name or ("self" if context is None else "cross")
     # 1. projections (library GEMMs)

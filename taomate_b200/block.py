@@ -32,6 +32,7 @@ learned-memory adapters, which no shipped inference config enables.
 
 from __future__ import annotations
 
+import contextlib
 from typing import Optional, Tuple
 
 import torch
@@ -40,9 +41,11 @@ from torch import Tensor
 
 from . import _lib
 from . import parallel as P
-from .attention import AttentionWeights, attention_with_cache, text_cross_attention_with_kv_cache
+from .attention import (AttentionWeights, _cache_source, _norm_eps, attention_with_cache,
+                        flash_attention, text_cross_attention_with_kv_cache)
 from .kv_cache import LayerKVCache, _cat_cache
 from .profiler import section
+from .rope import norm_rope
 
 # get_ada_values slices (causal_block.py:434-452): (shift, scale, gate) per sublayer
 _MSA = (0, 1, 2)
@@ -163,6 +166,54 @@ def feed_forward(ff, x: Tensor) -> Tensor:
     return F.linear(h, out.weight, out.bias)
 
 
+def video_to_audio_gathered(attn, ax_v2a: Tensor, vx_v2a: Tensor, audio_cross_pe, video_cross_pe,
+                            cached_k, cached_v, video_real_len: Optional[int] = None):
+    """V2A attention (audio queries over video keys) when the audio stream is
+    replicated on every rank and the video stream is split by sequence.
+
+    The reference moves Q, K and V seq->head and the output head->seq
+    (kv_cache.py:1432-1462, 1535-1538) over audio tokens padded to the rank
+    count.  Here each rank projects its own video tokens' K/V (norm + cross
+    RoPE fused, K and V interleaved per token) and one all-gather gives every
+    rank the chunk's K/V for all heads; the 25 audio queries then attend over
+    the cached and new video keys for all heads on every rank, so the output
+    is already replicated.  Cached and returned K/V hold all heads."""
+    import torch.distributed as dist
+    G, grp = P.get_sp_world_size(), P.get_sp_group()
+    H, D = int(attn.heads), int(attn.dim_head)
+    B, Lloc = int(vx_v2a.shape[0]), int(vx_v2a.shape[1])
+    if B != 1:
+        raise NotImplementedError("the gathered V2A path takes batch 1")
+    eps = _norm_eps(attn.q_norm)
+    with section("video_to_audio.qkv_proj_norm"):
+        q = F.linear(ax_v2a, attn.to_q.weight, attn.to_q.bias)
+        k = F.linear(vx_v2a, attn.to_k.weight, attn.to_k.bias)
+        v = F.linear(vx_v2a, attn.to_v.weight, attn.to_v.bias)
+    with section("video_to_audio.rope_reshape"):
+        (q,) = norm_rope([q], [attn.q_norm.weight], [audio_cross_pe], H, D, eps)
+        send = norm_rope([k, v], [attn.k_norm.weight, None], [video_cross_pe, None], H, D, eps,
+                         packed=True)  # [1, 1, Lloc, 2, H, D]
+    recv = torch.empty((G,) + tuple(send.shape[1:]), device=send.device, dtype=send.dtype)
+    with section("video_to_audio.all_gather"):
+        dist.all_gather_into_tensor(recv, send, group=grp)
+    flat = recv.view(G * Lloc, 2, H, D)
+    k_full, v_full = flat[:, 0].unsqueeze(0), flat[:, 1].unsqueeze(0)
+    n = G * Lloc
+    if video_real_len is not None and video_real_len < n:
+        n = int(video_real_len)
+        k_full, v_full = k_full[:, :n], v_full[:, :n]
+    ck, cv, spans = _cache_source(cached_k, cached_v)
+    with section("video_to_audio.sdpa"):
+        out = flash_attention(q, ck, cv, spans, k_full, v_full, n)
+    with section("video_to_audio.out_proj"):
+        out = out.reshape(B, -1, H * D)
+        if getattr(attn, "to_gate_logits", None) is not None:
+            gates = 2.0 * torch.sigmoid(attn.to_gate_logits(ax_v2a))
+            out = (out.view(B, -1, H, D) * gates.unsqueeze(-1)).view(B, -1, H * D)
+        out = attn.to_out(out)
+    return out, k_full, v_full
+
+
 def _ada(table, ts, L, n, D, frame_seqlen, offset):
     return AdaParams(table, ts, L, n, D, frame_seqlen, offset)
 
@@ -226,10 +277,19 @@ def block_forward_with_cache(
     *,
     video_token_offset: int = 0,
     audio_token_offset: int = 0,
+    audio_replicated: bool = False,
 ) -> Tuple[Tensor, Tensor, LayerKVCache]:
     """One block forward with KV cache (kv_cache.py:2145-2654); returns
     ``(video_x, audio_x, updated_layer_cache)``.  The inputs are not
-    modified."""
+    modified.
+
+    Under sequence parallelism the video stream is this rank's token shard
+    (``video_token_offset`` = its first token).  The audio stream is split
+    the same way (the reference's layout) unless ``audio_replicated``: then
+    every rank holds all audio tokens, the audio sublayers and A2V run
+    locally with all heads, V2A gathers the chunk's video K/V once
+    (:func:`video_to_audio_gathered`), and the audio, A2V and V2A caches hold
+    all heads."""
     if pyramid_policy is not None:
         raise NotImplementedError("pyramid KV selection is disabled in every shipped config")
     if getattr(block, "learned_memory_mode", None) is not None:
@@ -271,15 +331,18 @@ def block_forward_with_cache(
         prompt_cache_key=video_prompt_cache_key, cache_name="video_text_cross",
         layer_idx=layer_idx)
 
+    audio_local = audio_replicated and P.is_sp_enabled()
+    local = P.sp_local if audio_local else contextlib.nullcontext
     # ── audio self-attention (kv_cache.py:2464-2490)
     with section("block.audio_norm"):
         norm_ax = torch.empty_like(audio_x)
         residual_norm(audio_x, outs=[(norm_ax, asrc, _MSA[1], _MSA[0])], eps=eps)
-    ax_attn, new_as_k, new_as_v = attention_with_cache(
-        block.audio_attn1, norm_ax, None, audio_pe, None, layer_cache.audio_self_k,
-        layer_cache.audio_self_v, layer_idx=layer_idx, modality="audio",
-        frame_seqlen=audio_frame_seqlen, new_kv_real_len=audio_real_len,
-        profile_name="audio_self")
+    with local():
+        ax_attn, new_as_k, new_as_v = attention_with_cache(
+            block.audio_attn1, norm_ax, None, audio_pe, None, layer_cache.audio_self_k,
+            layer_cache.audio_self_v, layer_idx=layer_idx, modality="audio",
+            frame_seqlen=audio_frame_seqlen, new_kv_real_len=audio_real_len,
+            profile_name="audio_self")
     ax = torch.empty_like(audio_x)
     atin = torch.empty_like(audio_x)
     with section("block.audio_norm"):
@@ -320,14 +383,20 @@ def block_forward_with_cache(
         with section("block.audio_norm"):
             residual_norm(ax, a_text, tgate_a, _TEXT_Q[2], ax,
                           [(ax_a2v, aca, 0, 1), (ax_v2a, aca, 2, 3)], eps=eps)
-        a2v_out, new_a2v_k, new_a2v_v = attention_with_cache(
-            block.audio_to_video_attn, vx_a2v, ax_a2v, video_cross_pe, audio_cross_pe,
-            layer_cache.a2v_k, layer_cache.a2v_v, new_kv_real_len=audio_real_len,
-            profile_name="audio_to_video")
-        v2a_out, new_v2a_k, new_v2a_v = attention_with_cache(
-            block.video_to_audio_attn, ax_v2a, vx_v2a, audio_cross_pe, video_cross_pe,
-            layer_cache.v2a_k, layer_cache.v2a_v, new_kv_real_len=video_real_len,
-            profile_name="video_to_audio")
+        with local():  # replicated audio: this rank's video queries over all audio keys
+            a2v_out, new_a2v_k, new_a2v_v = attention_with_cache(
+                block.audio_to_video_attn, vx_a2v, ax_a2v, video_cross_pe, audio_cross_pe,
+                layer_cache.a2v_k, layer_cache.a2v_v, new_kv_real_len=audio_real_len,
+                profile_name="audio_to_video")
+        if audio_local:
+            v2a_out, new_v2a_k, new_v2a_v = video_to_audio_gathered(
+                block.video_to_audio_attn, ax_v2a, vx_v2a, audio_cross_pe, video_cross_pe,
+                layer_cache.v2a_k, layer_cache.v2a_v, video_real_len)
+        else:
+            v2a_out, new_v2a_k, new_v2a_v = attention_with_cache(
+                block.video_to_audio_attn, ax_v2a, vx_v2a, audio_cross_pe, video_cross_pe,
+                layer_cache.v2a_k, layer_cache.v2a_v, new_kv_real_len=video_real_len,
+                profile_name="video_to_audio")
         vg = _ada(block.scale_shift_table_a2v_ca_video[4:], video_cross_gate, Lv, 1, Dv,
                   video_frame_seqlen, video_token_offset)
         ag = _ada(block.scale_shift_table_a2v_ca_audio[4:], audio_cross_gate, La, 1, Da,

@@ -313,6 +313,18 @@ def _cat_cache(old, new: Tensor):
     return cat_tensors(old, new)
 
 
+def last_chunk(view_k: "ArenaKV") -> Tuple[Tensor, Tensor]:
+    """The ``(k, v)`` chunk most recently appended to an arena view pair and
+    not yet copied into a slot (a forward's new K/V, as ``_cat_cache``
+    recorded it)."""
+    if not isinstance(view_k, ArenaKV) or not view_k._state.pending:
+        raise ValueError("no pending chunk on this cache view")
+    k, v = view_k._state.pending[-1]
+    if v is None:
+        raise RuntimeError("K chunk appended without its V chunk")
+    return k, v
+
+
 def cat_cache_pair(old_k, old_v, new_k: Tensor, new_v: Tensor):
     """Append a K/V chunk to a pair of cache fields; returns ``(k, v)``."""
     return _cat_cache(old_k, new_k), _cat_cache(old_v, new_v)

@@ -28,6 +28,8 @@ with :func:`register_layout_copy`; the library registers none.
 
 from __future__ import annotations
 
+import contextlib
+
 import ctypes
 from typing import Callable, Dict, Optional, Sequence, Tuple
 
@@ -81,8 +83,26 @@ def get_device_mesh():
     return _DEVICE_MESH
 
 
+_SP_LOCAL = 0  # > 0 inside sp_local(): calls run as if sequence parallelism were off
+
+
 def is_sp_enabled() -> bool:
-    return _DEVICE_MESH is not None and _SP_SIZE > 1
+    return _DEVICE_MESH is not None and _SP_SIZE > 1 and _SP_LOCAL == 0
+
+
+@contextlib.contextmanager
+def sp_local():
+    """Run the enclosed calls as single-GPU calls on this rank's tensors even
+    though the SP mesh is set: for work every rank holds in full (the audio
+    stream, which a block replicates instead of splitting its 25 tokens) and
+    for attentions whose keys and values every rank already has.  Same role as
+    the reference's ``cp_disabled`` (ltx_causal/parallel/cp_utils.py:169-188)."""
+    global _SP_LOCAL
+    _SP_LOCAL += 1
+    try:
+        yield
+    finally:
+        _SP_LOCAL -= 1
 
 
 def get_sp_group():

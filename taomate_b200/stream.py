@@ -1,0 +1,266 @@
+"""Streaming generation on one rank: the block loop of the causal pipeline.
+
+Per block (taomate/inference/model.py:166-248, model_runtime.py:772-895):
+three denoising forwards over the block's noisy latents against the cached
+prefix (each followed by the Euler update of the latents), one sigma = 0
+commit forward whose new K/V are appended to every cache field, a segment
+record, then the streaming eviction (``retain_streaming_context``: sink
+segment + two newest, taomate/inference/cache.py:58-67), from
+``evict_from_block`` on.
+
+Execution: eager until the cache reaches its steady-state layout (sink + 2
+window blocks), then one forward is captured as a CUDA graph
+(:class:`taomate_b200.graphs.AttentionGraph`) and replayed for all four
+forwards of every later block; per block only the attention key-tile table
+(the new arena layout), the RoPE tables, the conditioning rows and the
+latents change, and each is written into the graph's own buffers by a kernel
+copy.  The text K/V of every layer are projected once per block by a second
+captured graph (the reference projects them in every forward unless its text
+K/V cache is on, which keeps them per prompt).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, fields
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+from . import parallel as P
+from .cache import attach_segments, cache_segments, retain_streaming_context
+from .graphs import AttentionGraph, attention_spans, copy_bytes
+from .kv_cache import FIELD_PAIRS, KVCache, LayerKVCache, cat_cache_pair, last_chunk
+from .model import (CausalModelWeights, Conditioning, StreamConfig, arena_cache, model_forward,
+                    rope_tables)
+from .rope import norm_rope
+
+# denoising sigmas of one block (taomate/inference/model.py:11-19), then 0
+SIGMAS = (1.0, 0.757, 0.522, 0.0)
+COND_FIELDS = ("video_ts", "audio_ts", "video_cross_ss", "video_cross_gate", "audio_cross_ss",
+               "audio_cross_gate", "video_emb2", "audio_emb2")
+
+
+def block_geometry(k: int, cfg: StreamConfig, first_frames: int = 4, frames: int = 3,
+                   audio_first: int = 26, audio: int = 25):
+    """(video frames, audio tokens, video start frame, audio start token) of
+    block ``k`` in the "4-3-3-3" layout (compute_av_blocks,
+    ltx_causal/attention/mask_builder.py:96-140)."""
+    if k == 0:
+        return first_frames, audio_first, 0, 0
+    return frames, audio, first_frames + frames * (k - 1), audio_first + audio * (k - 1)
+
+
+def _flat_nbytes(ts: Sequence[torch.Tensor]) -> int:
+    return sum((t.numel() * t.element_size() + 15) // 16 * 16 for t in ts)
+
+
+class StreamRunner:
+    """Runs blocks of one stream on this rank.  ``sp``/``rank``: the sequence
+    parallel layout (video tokens split, audio replicated)."""
+
+    def __init__(self, model: CausalModelWeights, device, sp: int = 1, rank: int = 0,
+                 graphed: bool = True, evict_from_block: int = 0, slots: int = 6):
+        self.model, self.cfg, self.dev = model, model.cfg, torch.device(device)
+        self.sp, self.rank, self.graphed = sp, rank, graphed
+        self.evict_from_block = evict_from_block
+        cfg = self.cfg
+        ff, fa, _, _ = block_geometry(0, cfg)
+        self.cache = arena_cache(cfg, ff * cfg.frame_tokens, fa, sp, slots, device=self.dev)
+        attach_segments(self.cache, [])
+        self.block = 0
+        self.graph: Optional[AttentionGraph] = None
+        self.text_graph: Optional[torch.cuda.CUDAGraph] = None
+        self.ctx = None  # (video_ctx, audio_ctx) of the current prompt
+        self.launches = 0
+
+    # -- geometry -------------------------------------------------------------
+    def local_tokens(self, frames: int) -> Tuple[int, int]:
+        L = frames * self.cfg.frame_tokens
+        if L % self.sp:
+            raise ValueError(f"{L} video tokens do not split over {self.sp} ranks")
+        n = L // self.sp
+        return n, self.rank * n
+
+    def steady(self) -> bool:
+        """The cache holds the sink block and two window blocks: every later
+        block sees the same number of key tiles per attention."""
+        return self.block >= max(3, self.evict_from_block + 3)
+
+    # -- one forward ------------------------------------------------------------
+    def _cond(self, c: Conditioning, pe) -> Conditioning:
+        vctx, actx = self.ctx
+        return Conditioning(**{f.name: getattr(c, f.name) for f in fields(Conditioning)
+                               if f.name not in ("pe", "video_ctx", "audio_ctx")},
+                            video_ctx=vctx, audio_ctx=actx, pe=pe)
+
+    def set_prompt(self, video_ctx: torch.Tensor, audio_ctx: torch.Tensor) -> None:
+        """New text conditioning (projected contexts ``[1, 256, D]``).  Kept in
+        fixed buffers so captured graphs read the current prompt."""
+        if self.ctx is None:
+            self.ctx = (video_ctx.clone(), audio_ctx.clone())
+        else:
+            self.ctx[0].copy_(video_ctx)
+            self.ctx[1].copy_(audio_ctx)
+        if self.text_graph is not None:
+            self.text_graph.replay()  # re-project into the entries the forward graph reads
+        else:
+            # the text K/V cache is keyed by the context tensor's identity, which
+            # stays: drop its entries so the next forward projects the new prompt
+            for blk in self.model.transformer_blocks:
+                for attn in (blk.attn2, blk.audio_attn2):
+                    if hasattr(attn, "_ltx_text_cross_kv_cache"):
+                        attn._ltx_text_cross_kv_cache.clear()
+
+    # -- the block ------------------------------------------------------------
+    def run_block(self, video_latent: torch.Tensor, audio_latent: torch.Tensor,
+                  conds: Sequence[Conditioning]) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Denoise the block's latents (``[1, Lv_local, C]``, ``[1, La, C]``)
+        with ``conds[0..2]``, commit with ``conds[3]``; returns the denoised
+        latents (fresh tensors)."""
+        if self.graphed and self.graph is None and self.steady():
+            self._capture(video_latent, audio_latent, conds)
+        if self.graph is not None:
+            return self._replay_block(video_latent, audio_latent, conds)
+        return self._eager_block(video_latent, audio_latent, conds)
+
+    def _pe(self, k: int):
+        F_, La, vs, as_ = block_geometry(k, self.cfg)
+        n, off = self.local_tokens(F_)
+        return rope_tables(self.cfg, F_, La, vs, as_, self.dev, slice(off, off + n)), off
+
+    def _commit(self, new_cache: KVCache) -> None:
+        F_, La, _, _ = block_geometry(self.block, self.cfg)
+        segs = cache_segments(self.cache) + [{"block_idx": self.block,
+                                              "video_tokens": F_ * self.cfg.frame_tokens,
+                                              "audio_tokens": La}]
+        attach_segments(new_cache, segs)
+        for lay in new_cache.layers:  # copy the pending chunks into their slots now
+            for kf, vf in FIELD_PAIRS:
+                getattr(lay, kf).entries()
+        if self.block >= self.evict_from_block and len(segs) > 3:
+            new_cache = retain_streaming_context(new_cache)
+        self.cache = new_cache
+        self.block += 1
+
+    def _eager_block(self, v, a, conds):
+        pe, off = self._pe(self.block)
+        x_v, x_a = v, a
+        with torch.no_grad():
+            for fwd in range(3):
+                vo, ao, _ = model_forward(self.model, x_v, x_a, self._cond(conds[fwd], pe),
+                                          self.cache, video_token_offset=off)
+                dt = SIGMAS[fwd + 1] - SIGMAS[fwd]
+                x_v = torch.add(x_v, vo, alpha=dt)  # the graph path's update, same rounding
+                x_a = torch.add(x_a, ao, alpha=dt)
+            _, _, new = model_forward(self.model, x_v, x_a, self._cond(conds[3], pe), self.cache,
+                                      kv_cache_only=True, video_token_offset=off)
+        self._commit(new)
+        return x_v, x_a
+
+    # -- graph executor -------------------------------------------------------
+    def _spans(self, cache: KVCache) -> List[List[Tuple[int, int, int]]]:
+        """Key spans of every attention site of a forward, in call order:
+        per layer video self, video text, audio self, audio text, A2V, V2A."""
+        F_, La, _, _ = block_geometry(self.block, self.cfg)
+        Lv = F_ * self.cfg.frame_tokens
+        text = [(0, 0, int(self.ctx[0].shape[1]))]
+        out = []
+        for lay in cache.layers:
+            out.append(attention_spans(lay.video_self_k, lay.video_self_v, Lv))
+            out.append(text)
+            out.append(attention_spans(lay.audio_self_k, lay.audio_self_v, La))
+            out.append([(0, 0, int(self.ctx[1].shape[1]))])
+            out.append(attention_spans(lay.a2v_k, lay.a2v_v, La))
+            out.append(attention_spans(lay.v2a_k, lay.v2a_v, Lv))
+        return out
+
+    def _capture(self, v, a, conds):
+        """Capture one steady-state forward (and the text K/V projection)."""
+        pe, off = self._pe(self.block)
+        self._static_pe = [t for pair in pe for t in pair]
+        cond0 = self._cond(conds[0], pe)
+        self._static_cond = [getattr(cond0, n).clone() for n in COND_FIELDS]
+        self._sv, self._sa = v.clone(), a.clone()
+        scond = Conditioning(**{n: t for n, t in zip(COND_FIELDS, self._static_cond)},
+                             video_ctx=self.ctx[0], audio_ctx=self.ctx[1], pe=pe)
+        for lay in self.cache.layers:  # pending chunks into their slots before capture
+            for kf, vf in FIELD_PAIRS:
+                getattr(lay, kf).entries()
+        # one eager forward first (cuBLAS / NCCL initialisation, text K/V cache warm)
+        with torch.no_grad():
+            model_forward(self.model, self._sv, self._sa, scond, self.cache,
+                          video_token_offset=off)
+        torch.cuda.synchronize(self.dev)
+        self.graph = AttentionGraph(self.dev, max_sites=6 * self.cfg.layers)
+        with torch.no_grad():
+            self._out_v, self._out_a, self._new = self.graph.capture(
+                model_forward, self.model, self._sv, self._sa, scond, self.cache,
+                video_token_offset=off)
+        self._chunks = [[last_chunk(getattr(lay, kf)) for kf, _ in FIELD_PAIRS]
+                        for lay in self._new.layers]
+        self._new = None  # its views would keep the capture-time slots referenced
+        self._capture_text()
+
+    def _capture_text(self):
+        """A graph that re-projects the text K/V of every layer into the
+        buffers the forward graph reads (the text K/V cache entries)."""
+        jobs = []
+        for blk in self.model.transformer_blocks:
+            for attn, ctx in ((blk.attn2, self.ctx[0]), (blk.audio_attn2, self.ctx[1])):
+                ent = [e for e in getattr(attn, "_ltx_text_cross_kv_cache", {}).values()
+                       if e[0]() is ctx]
+                if len(ent) != 1:
+                    raise RuntimeError("text K/V cache entry missing before capture")
+                jobs.append((attn, ctx, ent[0][1], ent[0][2]))
+        self._text_jobs = jobs
+        g = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(g):
+            self._project_text()
+        self.text_graph = g
+
+    def _project_text(self):
+        for attn, ctx, k, v in self._text_jobs:
+            H, D = int(attn.heads), int(attn.dim_head)
+            kp = F.linear(ctx, attn.to_k.weight, attn.to_k.bias)
+            (kn,) = norm_rope([kp], [attn.k_norm.weight], [None], H, D,
+                              float(attn.k_norm.eps or 1e-6))
+            k.copy_(kn)
+            v.copy_(F.linear(ctx, attn.to_v.weight, attn.to_v.bias).view_as(v))
+
+    def _load(self, dst: List[torch.Tensor], src: List[torch.Tensor]) -> None:
+        for d, s in zip(dst, src):
+            s = s if s.is_contiguous() else s.contiguous()
+            copy_bytes(d.data_ptr(), s.data_ptr(), (d.numel() * d.element_size() + 15) // 16 * 16,
+                       self.dev)
+
+    def _replay_block(self, v, a, conds):
+        pe, off = self._pe(self.block)
+        self._load(self._static_pe, [t for pair in pe for t in pair])
+        self._load([self._sv, self._sa], [v, a])
+        self.text_graph.replay()
+        spans = self._spans(self.cache)
+        for fwd in range(4):
+            self._load(self._static_cond, [getattr(conds[fwd], n) for n in COND_FIELDS])
+            self.graph.replay(spans if fwd == 0 else None)
+            if fwd < 3:
+                dt = SIGMAS[fwd + 1] - SIGMAS[fwd]
+                self._sv.add_(self._out_v, alpha=dt)
+                self._sa.add_(self._out_a, alpha=dt)
+        # commit: this block's K/V (the fourth replay's) appended to the cache
+        layers = []
+        for lay, chunks in zip(self.cache.layers, self._chunks):
+            kw = {}
+            for (kf, vf), (nk, nv) in zip(FIELD_PAIRS, chunks):
+                kw[kf], kw[vf] = cat_cache_pair(getattr(lay, kf), getattr(lay, vf), nk, nv)
+            layers.append(LayerKVCache(**kw))
+        self._commit(KVCache(layers=layers))
+        return self._sv.clone(), self._sa.clone()
+
+    def release(self):
+        """Drop the captured graphs (before the process group goes away)."""
+        if self.graph is not None:
+            self.graph.reset()
+        self.graph = None
+        self.text_graph = None

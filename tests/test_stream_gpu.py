@@ -1,0 +1,77 @@
+"""The streaming block loop (taomate_b200.stream.StreamRunner) on one GPU.
+
+A 2-layer model at small shapes (video 4 heads x 128 over 8 x 12 tokens per
+frame, audio 4 heads x 64, text 24 tokens) runs the pipeline's schedule:
+block 0 of 4 frames, then blocks of 3 frames, each with 3 denoising forwards
+and a commit forward, eviction to the sink block + the 2 newest blocks.
+
+* The CUDA-graph executor (capture at the steady state, replay with a
+  rewritten key-tile table, kernel-copied inputs, per-block text K/V graph)
+  gives the same bits as issuing every forward eagerly.
+* The retained segments follow the reference policy ([0], [0,1], [0,1,2],
+  [0,2,3], [0,3,4], ...) and the cache holds 3840-equivalent rows (sink + 2
+  blocks) at the steady state.
+* A prompt change reaches the captured graph (the outputs change and match
+  the eager run with the same prompt change).
+"""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda:0") if torch.cuda.is_available() else None
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _device():
+    if DEV is None:
+        pytest.skip("no CUDA device")
+    torch.cuda.set_device(DEV)
+    yield
+    from taomate_b200 import _lib
+    assert _lib.device_error() == 0, "a kernel set the device error flag"
+
+
+def _run(graphed, n_blocks=7, prompt_change_at=5):
+    from taomate_b200.model import CausalModelWeights, StreamConfig, synthetic_conditioning
+    from taomate_b200.stream import StreamRunner, block_geometry
+    cfg = StreamConfig(layers=2, video_dim=512, video_heads=4, video_dim_head=128, audio_dim=256,
+                       audio_heads=4, audio_dim_head=64, frame_h=8, frame_w=12, text_tokens=24)
+    torch.manual_seed(0)
+    model = CausalModelWeights(cfg, device=DEV, std=0.05)
+    gen = torch.Generator(device=DEV).manual_seed(3)
+    runner = StreamRunner(model, DEV, graphed=graphed)
+    p0 = synthetic_conditioning(cfg, 3, 25, DEV, gen)
+    p1 = synthetic_conditioning(cfg, 3, 25, DEV, gen)
+    runner.set_prompt(p0.video_ctx, p0.audio_ctx)
+    outs, kept = [], []
+    for k in range(n_blocks):
+        if k == prompt_change_at:
+            runner.set_prompt(p1.video_ctx, p1.audio_ctx)
+        F_, La, _, _ = block_geometry(k, cfg)
+        v = torch.randn(1, F_ * cfg.frame_tokens, cfg.in_channels, device=DEV,
+                        generator=gen).to(torch.bfloat16)
+        a = torch.randn(1, La, cfg.in_channels, device=DEV, generator=gen).to(torch.bfloat16)
+        conds = [synthetic_conditioning(cfg, F_, La, DEV, gen) for _ in range(4)]
+        vo, ao = runner.run_block(v, a, conds)
+        outs.append((vo.clone(), ao.clone()))
+        kept.append([s["block_idx"] for s in runner.cache.segments])
+    torch.cuda.synchronize()
+    rows = int(runner.cache.layers[0].video_self_k.shape[1])
+    captured = runner.graph is not None
+    runner.release()
+    return outs, kept, rows, captured
+
+
+def test_graph_executor_equals_eager():
+    eo, ek, erows, ecap = _run(graphed=False)
+    go, gk, grows, gcap = _run(graphed=True)
+    assert not ecap and gcap
+    assert ek == gk == [[0], [0, 1], [0, 1, 2], [0, 2, 3], [0, 3, 4], [0, 4, 5], [0, 5, 6]]
+    assert erows == grows == (4 + 3 + 3) * 96
+    for i, ((ev, ea), (gv, ga)) in enumerate(zip(eo, go)):
+        assert torch.equal(ev, gv), f"video output of block {i}"
+        assert torch.equal(ea, ga), f"audio output of block {i}"
+    # the prompt change at block 5 is visible
+    assert not torch.equal(go[5][0], go[4][0])
