@@ -80,6 +80,9 @@ def parse():
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--heads", type=int, default=None,
                     help="--kernel-case attention: heads per GPU (32 / sequence-parallel ranks)")
+    ap.add_argument("--cached", type=int, default=None,
+                    help="--kernel-case attention: cached keys (3456: config 2; 3840: the "
+                         "production layout of the C4 step)")
     return ap.parse_args()
 
 
@@ -948,7 +951,7 @@ def run_kernel_case(args):
     torch.cuda.set_device(dev)
     g = torch.Generator(device=dev).manual_seed(0)
     Lq = Q_FRAMES * FRAME_TOKENS
-    Lc = (ANCHOR_FRAMES + WINDOW_FRAMES) * FRAME_TOKENS
+    Lc = args.cached or (ANCHOR_FRAMES + WINDOW_FRAMES) * FRAME_TOKENS
     rnd = lambda *s: torch.randn(*s, device=dev, generator=g).to(torch.bfloat16)
     if args.kernel_case == "attention":
         Hk = args.heads or HEADS
@@ -997,6 +1000,7 @@ def run_kernel_case(args):
     ms = sorted(a.elapsed_time(b) for a, b in ev)
     med = ms[len(ms) // 2]
     print(json.dumps({"kernel_case": args.kernel_case, "heads": args.heads or HEADS,
+                      "cached": Lc,
                       "median_ms": med, "min_ms": ms[0],
                       "achieved": work / (med * 1e-3), "unit": unit}), flush=True)
 

@@ -113,7 +113,8 @@ def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tens
     rec = _graphs.recorder()
     if rec is not None:
         # captured into a graph: the key-tile list goes to the graph's device table
-        ext.device_tiles = rec._add_site(arr, len(spans), crows, nrows)
+        ext.device_tiles = rec._add_site(arr, len(spans), crows, nrows,
+                                         cache_k.data_ptr() if cache_k is not None else None)
     with torch.cuda.device(dev):
         _lib.check(lib.tm_attention_fwd_ext(
             q.data_ptr(), qbs, qrs,

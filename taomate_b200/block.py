@@ -214,6 +214,16 @@ def video_to_audio_gathered(attn, ax_v2a: Tensor, vx_v2a: Tensor, audio_cross_pe
     return out, k_full, v_full
 
 
+_AUDIO_STREAMS = {}
+
+
+def _audio_stream(dev: torch.device) -> torch.cuda.Stream:
+    st = _AUDIO_STREAMS.get(dev.index)
+    if st is None:
+        st = _AUDIO_STREAMS[dev.index] = torch.cuda.Stream(dev)
+    return st
+
+
 def _ada(table, ts, L, n, D, frame_seqlen, offset):
     return AdaParams(table, ts, L, n, D, frame_seqlen, offset)
 
@@ -278,6 +288,7 @@ def block_forward_with_cache(
     video_token_offset: int = 0,
     audio_token_offset: int = 0,
     audio_replicated: bool = False,
+    overlap_audio: bool = True,
 ) -> Tuple[Tensor, Tensor, LayerKVCache]:
     """One block forward with KV cache (kv_cache.py:2145-2654); returns
     ``(video_x, audio_x, updated_layer_cache)``.  The inputs are not
@@ -289,7 +300,8 @@ def block_forward_with_cache(
     every rank holds all audio tokens, the audio sublayers and A2V run
     locally with all heads, V2A gathers the chunk's video K/V once
     (:func:`video_to_audio_gathered`), and the audio, A2V and V2A caches hold
-    all heads."""
+    all heads.  ``overlap_audio`` runs the audio chain on a second stream
+    beside the video chain (same kernels, same results)."""
     if pyramid_policy is not None:
         raise NotImplementedError("pyramid KV selection is disabled in every shipped config")
     if getattr(block, "learned_memory_mode", None) is not None:
@@ -304,6 +316,45 @@ def block_forward_with_cache(
                 video_token_offset)
     asrc = _ada(block.audio_scale_shift_table, audio_timestep_6d, La, n_ada, Da,
                 audio_frame_seqlen, audio_token_offset)
+
+    # Two chains meet only at the cross-modal norms: the video chain (self,
+    # text, A2V, FFN) runs on the current stream, the audio chain (self, text,
+    # V2A, FFN: 25-token kernels bound by latency and weight reads) on a side
+    # stream beside it, inside a captured graph too.  Every tensor either
+    # chain touches stays referenced until the streams join at the end.
+    main = torch.cuda.current_stream(video_x.device)
+    side = _audio_stream(video_x.device) if overlap_audio else main
+    side.wait_stream(main)
+    audio_local = audio_replicated and P.is_sp_enabled()
+    local = P.sp_local if audio_local else contextlib.nullcontext
+
+    # ── audio self-attention (kv_cache.py:2464-2490) + audio text cross (:2493-2510)
+    with torch.cuda.stream(side):
+        with section("block.audio_norm"):
+            norm_ax = torch.empty_like(audio_x)
+            residual_norm(audio_x, outs=[(norm_ax, asrc, _MSA[1], _MSA[0])], eps=eps)
+        with local():
+            ax_attn, new_as_k, new_as_v = attention_with_cache(
+                block.audio_attn1, norm_ax, None, audio_pe, None, layer_cache.audio_self_k,
+                layer_cache.audio_self_v, layer_idx=layer_idx, modality="audio",
+                frame_seqlen=audio_frame_seqlen, new_kv_real_len=audio_real_len,
+                profile_name="audio_self")
+        ax = torch.empty_like(audio_x)
+        atin = torch.empty_like(audio_x)
+        with section("block.audio_norm"):
+            if block.cross_attention_adaln:
+                residual_norm(audio_x, ax_attn, asrc, _MSA[2], ax,
+                              [(atin, asrc, _TEXT_Q[1], _TEXT_Q[0])], eps=eps)
+            else:
+                residual_norm(audio_x, ax_attn, asrc, _MSA[2], ax, [(atin, None, -1, -1)],
+                              eps=eps)
+        a_ctx = _text_context(block, audio_ctx,
+                              getattr(block, "audio_prompt_scale_shift_table", None),
+                              audio_prompt_ts)
+        a_text = text_cross_attention_with_kv_cache(
+            block.audio_attn2, atin, a_ctx, mask=audio_context_mask, base_context=audio_ctx,
+            prompt_cache_key=audio_prompt_cache_key, cache_name="audio_text_cross",
+            layer_idx=layer_idx)
 
     # ── video self-attention (kv_cache.py:2197-2218)
     with section("block.video_norm"):
@@ -330,34 +381,7 @@ def block_forward_with_cache(
         block.attn2, tin, v_ctx, mask=video_context_mask, base_context=video_ctx,
         prompt_cache_key=video_prompt_cache_key, cache_name="video_text_cross",
         layer_idx=layer_idx)
-
-    audio_local = audio_replicated and P.is_sp_enabled()
-    local = P.sp_local if audio_local else contextlib.nullcontext
-    # ── audio self-attention (kv_cache.py:2464-2490)
-    with section("block.audio_norm"):
-        norm_ax = torch.empty_like(audio_x)
-        residual_norm(audio_x, outs=[(norm_ax, asrc, _MSA[1], _MSA[0])], eps=eps)
-    with local():
-        ax_attn, new_as_k, new_as_v = attention_with_cache(
-            block.audio_attn1, norm_ax, None, audio_pe, None, layer_cache.audio_self_k,
-            layer_cache.audio_self_v, layer_idx=layer_idx, modality="audio",
-            frame_seqlen=audio_frame_seqlen, new_kv_real_len=audio_real_len,
-            profile_name="audio_self")
-    ax = torch.empty_like(audio_x)
-    atin = torch.empty_like(audio_x)
-    with section("block.audio_norm"):
-        if block.cross_attention_adaln:
-            residual_norm(audio_x, ax_attn, asrc, _MSA[2], ax,
-                          [(atin, asrc, _TEXT_Q[1], _TEXT_Q[0])], eps=eps)
-        else:
-            residual_norm(audio_x, ax_attn, asrc, _MSA[2], ax, [(atin, None, -1, -1)], eps=eps)
-    # ── audio text cross-attention (kv_cache.py:2493-2510)
-    a_ctx = _text_context(block, audio_ctx, getattr(block, "audio_prompt_scale_shift_table", None),
-                          audio_prompt_ts)
-    a_text = text_cross_attention_with_kv_cache(
-        block.audio_attn2, atin, a_ctx, mask=audio_context_mask, base_context=audio_ctx,
-        prompt_cache_key=audio_prompt_cache_key, cache_name="audio_text_cross",
-        layer_idx=layer_idx)
+    main.wait_stream(side)
 
     # the text cross residuals (gate 6:9 under cross_attention_adaln, none
     # otherwise), fused with the norms that follow
@@ -383,29 +407,34 @@ def block_forward_with_cache(
         with section("block.audio_norm"):
             residual_norm(ax, a_text, tgate_a, _TEXT_Q[2], ax,
                           [(ax_a2v, aca, 0, 1), (ax_v2a, aca, 2, 3)], eps=eps)
-        with local():  # replicated audio: this rank's video queries over all audio keys
-            a2v_out, new_a2v_k, new_a2v_v = attention_with_cache(
-                block.audio_to_video_attn, vx_a2v, ax_a2v, video_cross_pe, audio_cross_pe,
-                layer_cache.a2v_k, layer_cache.a2v_v, new_kv_real_len=audio_real_len,
-                profile_name="audio_to_video")
-        if audio_local:
-            v2a_out, new_v2a_k, new_v2a_v = video_to_audio_gathered(
-                block.video_to_audio_attn, ax_v2a, vx_v2a, audio_cross_pe, video_cross_pe,
-                layer_cache.v2a_k, layer_cache.v2a_v, video_real_len)
-        else:
-            v2a_out, new_v2a_k, new_v2a_v = attention_with_cache(
-                block.video_to_audio_attn, ax_v2a, vx_v2a, audio_cross_pe, video_cross_pe,
-                layer_cache.v2a_k, layer_cache.v2a_v, new_kv_real_len=video_real_len,
-                profile_name="video_to_audio")
         vg = _ada(block.scale_shift_table_a2v_ca_video[4:], video_cross_gate, Lv, 1, Dv,
                   video_frame_seqlen, video_token_offset)
         ag = _ada(block.scale_shift_table_a2v_ca_audio[4:], audio_cross_gate, La, 1, Da,
                   audio_frame_seqlen, audio_token_offset)
-        # gated cross-modal residuals + the FFN inputs (slice 3:6)
+        side.wait_stream(main)
+        # audio chain: V2A, gated residual + FFN input (slice 3:6), FFN
+        with torch.cuda.stream(side):
+            if audio_local:
+                v2a_out, new_v2a_k, new_v2a_v = video_to_audio_gathered(
+                    block.video_to_audio_attn, ax_v2a, vx_v2a, audio_cross_pe, video_cross_pe,
+                    layer_cache.v2a_k, layer_cache.v2a_v, video_real_len)
+            else:
+                v2a_out, new_v2a_k, new_v2a_v = attention_with_cache(
+                    block.video_to_audio_attn, ax_v2a, vx_v2a, audio_cross_pe, video_cross_pe,
+                    layer_cache.v2a_k, layer_cache.v2a_v, new_kv_real_len=video_real_len,
+                    profile_name="video_to_audio")
+            with section("block.audio_norm"):
+                residual_norm(ax, v2a_out, ag, 0, ax, [(ffin_a, asrc, _MLP[1], _MLP[0])],
+                              eps=eps)
+        # video chain: A2V (replicated audio: this rank's video queries over all
+        # audio keys), gated residual + FFN input
+        with local():
+            a2v_out, new_a2v_k, new_a2v_v = attention_with_cache(
+                block.audio_to_video_attn, vx_a2v, ax_a2v, video_cross_pe, audio_cross_pe,
+                layer_cache.a2v_k, layer_cache.a2v_v, new_kv_real_len=audio_real_len,
+                profile_name="audio_to_video")
         with section("block.video_norm"):
             residual_norm(vx, a2v_out, vg, 0, vx, [(ffin_v, vsrc, _MLP[1], _MLP[0])], eps=eps)
-        with section("block.audio_norm"):
-            residual_norm(ax, v2a_out, ag, 0, ax, [(ffin_a, asrc, _MLP[1], _MLP[0])], eps=eps)
     else:
         with section("block.video_norm"):
             residual_norm(vx, v_text, tgate_v, _TEXT_Q[2], vx,
@@ -413,14 +442,17 @@ def block_forward_with_cache(
         with section("block.audio_norm"):
             residual_norm(ax, a_text, tgate_a, _TEXT_Q[2], ax,
                           [(ffin_a, asrc, _MLP[1], _MLP[0])], eps=eps)
+        side.wait_stream(main)
 
     # ── FFNs (kv_cache.py:2600-2640)
+    with torch.cuda.stream(side):
+        with section("block.audio_ff"):
+            a_ff = feed_forward(block.audio_ff, ffin_a)
+            residual_norm(ax, a_ff, asrc, _MLP[2], ax, eps=eps)
     with section("block.video_ff"):
         v_ff = feed_forward(block.ff, ffin_v)
         residual_norm(vx, v_ff, vsrc, _MLP[2], vx, eps=eps)
-    with section("block.audio_ff"):
-        a_ff = feed_forward(block.audio_ff, ffin_a)
-        residual_norm(ax, a_ff, asrc, _MLP[2], ax, eps=eps)
+    main.wait_stream(side)
 
     # ── cache update (kv_cache.py:2642-2654)
     keep = lambda old, new: _cat_cache(old, new) if new is not None else old

@@ -81,8 +81,9 @@ __device__ __forceinline__ void param8(const Src& s, int p, int D, int b, int t,
     for (int i = 0; i < 8; ++i) out[i] += tmp[i];
   }
   if (s.ts) {
-    const int64_t row = (t + s.ts_off) / s.ts_div;
-    bf8_to_f32(__ldg(reinterpret_cast<const uint4*>(s.ts + b * s.ts_bs + row * s.ts_rs +
+    const int row = (t + s.ts_off) / s.ts_div;  // 32-bit: token and frame indices fit
+    bf8_to_f32(__ldg(reinterpret_cast<const uint4*>(s.ts + b * s.ts_bs +
+                                                    static_cast<int64_t>(row) * s.ts_rs +
                                                     static_cast<int64_t>(p) * D + c)),
                tmp);
 #pragma unroll

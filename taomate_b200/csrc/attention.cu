@@ -784,15 +784,25 @@ static int sm_count() {
   return counts[dev];
 }
 
+// One unit = one query tile against all visible keys with both softmax lanes
+// splitting the key tiles (n_tiles / 2 lane steps).  Every CTA also pays a
+// fixed cost (TMEM allocation, barrier setup, the Q load, the epilogue)
+// worth kFixedLaneSteps key-tile steps of one lane, so splitting a tiny query
+// chunk into many short CTAs (V2A's 25 audio queries) stops paying off once
+// the splits fill one wave.
+constexpr double kFixedLaneSteps = 6.0;
+
 static Plan make_plan(int B, int Lq, int H, int D, int n_tiles, int64_t ws_bytes) {
   const int sms = sm_count();
   const int64_t nq = (Lq + BM - 1) / BM;
   const int64_t heads = static_cast<int64_t>(H) * B;
   const int64_t big = heads * (nq / 2), small = heads * (nq & 1);
+  const double c0 = kFixedLaneSteps / std::max(1.0, 0.5 * n_tiles);  // in units
+  const auto waves = [sms](int64_t ctas) { return static_cast<double>((ctas + sms - 1) / sms); };
   // pair mode: 2-unit CTAs, then 1-unit CTAs
-  const int64_t waves_big = (big + sms - 1) / sms;
-  const double cost_pair =
-      std::max(2.0 * waves_big, std::ceil(static_cast<double>(2 * big + small) / sms));
+  const double cost_pair = std::max(waves(big) * (2.0 + c0),
+                                    std::ceil(static_cast<double>(2 * big + small) / sms) +
+                                        c0 * waves(big + small));
   Plan best{0, 1};
   double best_cost = cost_pair;
   const int s_max = std::max(1, std::min(32, n_tiles / 2));
@@ -800,7 +810,7 @@ static Plan make_plan(int B, int Lq, int H, int D, int n_tiles, int64_t ws_bytes
     if (s > 1 && split_ws_bytes(s, B, Lq, H, D) > ws_bytes) break;
     const int64_t ctas = heads * nq * s;
     // the merge pass of s > 1 costs a little: require a clear gain
-    const double cost = std::ceil(static_cast<double>(ctas) / sms) / s * (s > 1 ? 1.08 : 1.0);
+    const double cost = waves(ctas) * (1.0 / s + c0) * (s > 1 ? 1.08 : 1.0);
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
       best = Plan{1, s};

@@ -42,11 +42,12 @@ def recorder() -> Optional["AttentionGraph"]:
 
 
 class _Site:
-    __slots__ = ("offset", "n_tiles", "cache_rows", "new_rows")
+    __slots__ = ("offset", "n_tiles", "cache_rows", "new_rows", "key")
 
-    def __init__(self, offset, n_tiles, cache_rows, new_rows):
+    def __init__(self, offset, n_tiles, cache_rows, new_rows, key=None):
         self.offset, self.n_tiles = offset, n_tiles
         self.cache_rows, self.new_rows = cache_rows, new_rows
+        self.key = key
 
 
 class AttentionGraph:
@@ -95,15 +96,17 @@ class AttentionGraph:
         self._dirty = True  # the capture-time tile lists are staged, not yet copied
         return out
 
-    def _add_site(self, spans, n_spans: int, cache_rows: int, new_rows: int) -> int:
+    def _add_site(self, spans, n_spans: int, cache_rows: int, new_rows: int,
+                  key: Optional[int] = None) -> int:
         """Called by flash_attention while capturing: stage this call's tile
-        list and return the device address its kernel reads."""
+        list and return the device address its kernel reads.  ``key`` names
+        the site for ``replay`` (the cache source's base address)."""
         if len(self.sites) >= self.max_sites:
             raise RuntimeError(f"more than {self.max_sites} attention calls in one graph")
         offset = self._used
         n = self._write_tiles(self._stage[self._cur], offset, spans, n_spans, cache_rows,
                               new_rows)
-        self.sites.append(_Site(offset, n, cache_rows, new_rows))
+        self.sites.append(_Site(offset, n, cache_rows, new_rows, key))
         step = (n + _SITE_ALIGN - 1) // _SITE_ALIGN * _SITE_ALIGN
         self._used = offset + 2 * max(step, _SITE_ALIGN)
         return self.table.data_ptr() + offset * 4
@@ -119,19 +122,32 @@ class AttentionGraph:
         return n.value
 
     # -- replay ------------------------------------------------------------
-    def replay(self, site_spans: Optional[Sequence[Sequence[Tuple[int, int, int]]]] = None):
+    def replay(self, site_spans=None):
+        """Replay the graph.  ``site_spans``: None (keep the tables), a list
+        with one span list per site in call order, or a dict from a site's key
+        (its cache source's base address) to its span list; sites not in the
+        dict keep their current table."""
         if self.graph is None:
             raise RuntimeError("nothing captured")
         stream = torch.cuda.current_stream(self.device)
         if site_spans is not None:
-            if len(site_spans) != len(self.sites):
-                raise ValueError(f"{len(site_spans)} span lists for {len(self.sites)} sites")
             nxt = 1 - self._cur
             ev = self._events[nxt]
             if ev is not None:
                 ev.synchronize()  # its previous copy to the table has run
             buf = self._stage[nxt]
-            for site, spans in zip(self.sites, site_spans):
+            if isinstance(site_spans, dict):
+                buf[:self._used].copy_(self._stage[self._cur][:self._used])
+                pairs = [(site, site_spans[site.key]) for site in self.sites
+                         if site.key in site_spans]
+                covered = {site.key for site, _ in pairs}
+                if set(site_spans) - covered:
+                    raise ValueError("span lists for keys no site was captured with")
+            else:
+                if len(site_spans) != len(self.sites):
+                    raise ValueError(f"{len(site_spans)} span lists for {len(self.sites)} sites")
+                pairs = list(zip(self.sites, site_spans))
+            for site, spans in pairs:
                 arr = (_lib.KVSpan * max(1, len(spans)))()
                 for i, (src, s, r) in enumerate(spans):
                     arr[i].source, arr[i].row_start, arr[i].rows = int(src), int(s), int(r)

@@ -160,20 +160,16 @@ class StreamRunner:
         return x_v, x_a
 
     # -- graph executor -------------------------------------------------------
-    def _spans(self, cache: KVCache) -> List[List[Tuple[int, int, int]]]:
-        """Key spans of every attention site of a forward, in call order:
-        per layer video self, video text, audio self, audio text, A2V, V2A."""
+    def _spans(self, cache: KVCache):
+        """Key spans of every cached attention of a forward, keyed by the
+        site's cache arena (the text cross-attention sites keep theirs)."""
         F_, La, _, _ = block_geometry(self.block, self.cfg)
         Lv = F_ * self.cfg.frame_tokens
-        text = [(0, 0, int(self.ctx[0].shape[1]))]
-        out = []
+        out = {}
         for lay in cache.layers:
-            out.append(attention_spans(lay.video_self_k, lay.video_self_v, Lv))
-            out.append(text)
-            out.append(attention_spans(lay.audio_self_k, lay.audio_self_v, La))
-            out.append([(0, 0, int(self.ctx[1].shape[1]))])
-            out.append(attention_spans(lay.a2v_k, lay.a2v_v, La))
-            out.append(attention_spans(lay.v2a_k, lay.v2a_v, Lv))
+            for (kf, vf), new_rows in zip(FIELD_PAIRS, (Lv, La, La, Lv)):
+                k, v = getattr(lay, kf), getattr(lay, vf)
+                out[k.arena.k.data_ptr()] = attention_spans(k, v, new_rows)
         return out
 
     def _capture(self, v, a, conds):

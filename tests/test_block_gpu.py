@@ -132,6 +132,26 @@ def test_block_adaln_rows_per_frame_equal_per_token():
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
 
 
+def test_block_audio_stream_overlap_same_bits():
+    """The audio chain on its own stream (the default) gives the bits of the
+    one-stream schedule."""
+    from taomate_b200.block import block_forward_with_cache
+    d = inputs.block_case_inputs("small")
+    blk, x, pes, mask, lc = _setup(d)
+    a = _run(blk, x, pes, mask, lc, d["frame_seqlen"])
+    fs = d["frame_seqlen"]
+    vpe, ape, vcpe, acpe = pes
+    with torch.no_grad():
+        b = block_forward_with_cache(
+            blk, x["video_x"], x["audio_x"], x["video_ts"], x["audio_ts"], vpe, ape, vcpe, acpe,
+            x["video_ctx"], x["audio_ctx"], mask, mask, x["video_cross_ss"],
+            x["video_cross_gate"], x["audio_cross_ss"], x["audio_cross_gate"], None, None, None,
+            None, lc, layer_idx=0, video_frame_seqlen=fs, audio_frame_seqlen=1,
+            overlap_audio=False)
+    torch.cuda.synchronize()
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
 def test_block_arena_caches_equal_plain_caches():
     d = inputs.block_case_inputs("small")
     blk, x, pes, mask, lc = _setup(d)

@@ -89,10 +89,63 @@ def _worker(rank, world, port, outdir):
             out_f, nk_f, nv_f = tm.attention_with_cache(
                 attn, x[:, ts].contiguous(), None, (cos[:, :, ts], sin[:, :, ts]), None,
                 ck[:, :, hs].contiguous(), cv[:, :, hs].contiguous())
+        # the whole block (small shapes): video split by tokens, audio replicated,
+        # text cross-attention over all heads locally, V2A with one all-gather
+        from taomate_b200.block import BlockWeights
+        from taomate_b200.kv_cache import LayerKVCache
+        from taomate_b200.model import StreamConfig, rope_tables, synthetic_conditioning
+        cfg = StreamConfig(layers=1, video_dim=hidden, video_heads=heads, video_dim_head=dim_head,
+                           audio_dim=256, audio_heads=4, audio_dim_head=64, frame_h=fh,
+                           frame_w=fw, text_tokens=24)
+        torch.manual_seed(4)
+        blk = BlockWeights(hidden, heads, dim_head, 256, 4, 64, device=dev, std=0.05)
+        cond = synthetic_conditioning(cfg, frames, 16, dev, g)
+        vx = torch.randn(1, lq, hidden, device=dev, generator=g).to(torch.bfloat16)
+        ax = torch.randn(1, 16, 256, device=dev, generator=g).to(torch.bfloat16)
+        rnd = lambda *s_: torch.randn(*s_, device=dev, generator=g).to(torch.bfloat16)
+        caches = {"video_self": (rnd(1, lc, heads, dim_head), rnd(1, lc, heads, dim_head)),
+                  "audio_self": (rnd(1, 32, 4, 64), rnd(1, 32, 4, 64)),
+                  "a2v": (rnd(1, 32, 4, 64), rnd(1, 32, 4, 64)),
+                  "v2a": (rnd(1, lc, 4, 64), rnd(1, lc, 4, 64))}
+
+        def lcache(shard):
+            kw = {}
+            for nm, (k_, v_) in caches.items():
+                if shard and nm == "video_self":
+                    k_, v_ = k_[:, :, hs].contiguous(), v_[:, :, hs].contiguous()
+                kw[nm + "_k"], kw[nm + "_v"] = k_, v_
+            return LayerKVCache(**kw)
+
+        def bargs(pe, off, rep, shard):
+            return dict(video_timestep_6d=cond.video_ts, audio_timestep_6d=cond.audio_ts,
+                        video_pe=pe[0], audio_pe=pe[1], video_cross_pe=pe[2],
+                        audio_cross_pe=pe[3], video_ctx=cond.video_ctx, audio_ctx=cond.audio_ctx,
+                        video_context_mask=None, audio_context_mask=None,
+                        video_cross_ss=cond.video_cross_ss,
+                        video_cross_gate=cond.video_cross_gate,
+                        audio_cross_ss=cond.audio_cross_ss,
+                        audio_cross_gate=cond.audio_cross_gate, video_prompt_ts=None,
+                        audio_prompt_ts=None, layer_cache=lcache(shard),
+                        video_frame_seqlen=fh * fw, audio_frame_seqlen=1,
+                        video_token_offset=off, audio_replicated=rep)
+
+        with torch.no_grad():
+            with P.sp_local():
+                rv, ra, rc = tm.block_forward_with_cache(
+                    blk, vx, ax, **bargs(rope_tables(cfg, frames, 16, 3, 26, dev), 0, False,
+                                         False))
+            bv, ba, bc = tm.block_forward_with_cache(
+                blk, vx[:, ts].contiguous(), ax,
+                **bargs(rope_tables(cfg, frames, 16, 3, 26, dev, ts), rank * sl, True, True))
         torch.cuda.synchronize()
         code = ctypes.c_int(0)
         assert _lib.load().tm_device_error(ctypes.byref(code)) == 0 and code.value == 0
         P.close_peer_exchange()
+        f = lambda t: t.float().cpu().numpy()
+        np.savez(os.path.join(outdir, f"b{rank}.npz"), vx=f(bv), ref_vx=f(rv[:, ts]), ax=f(ba),
+                 ref_ax=f(ra), vs_k=f(bc.video_self_k[:, lc:]), ref_vs_k=f(rc.video_self_k[:, lc:, hs]),
+                 v2a_k=f(bc.v2a_k[:, lc:]), ref_v2a_k=f(rc.v2a_k[:, lc:]),
+                 a2v_k=f(bc.a2v_k[:, 32:]), ref_a2v_k=f(rc.a2v_k[:, 32:]))
         f = lambda t: t.float().cpu().numpy()
         np.savez(os.path.join(outdir, f"r{rank}.npz"), out=f(out), ref_out=f(ref_out[:, ts]),
                  k=f(nk), ref_k=f(ref_k[:, :, hs]), v=f(nv), ref_v=f(ref_v[:, :, hs]),
@@ -131,3 +184,11 @@ def test_ulysses_sp_matches_single_gpu(tmp_path, world):
         # fused QKV projection: another GEMM kernel, the same arithmetic after it
         assert _rel_l2(z["out_f"], z["out_p"]) < 1e-2
         assert _rel_l2(z["k_f"], z["k_p"]) < 5e-3 and _rel_l2(z["v_f"], z["v_p"]) < 5e-3
+        # the block: same bar as the attention call (projection rounding on 1/G of the rows)
+        b = np.load(tmp_path / f"b{r}.npz")
+        assert b["vx"].shape == b["ref_vx"].shape and b["ax"].shape == b["ref_ax"].shape
+        assert _rel_l2(b["vx"], b["ref_vx"]) < 1e-2
+        assert _rel_l2(b["ax"], b["ref_ax"]) < 1e-2  # replicated audio: every rank's full output
+        assert _rel_l2(b["vs_k"], b["ref_vs_k"]) < 5e-3
+        assert _rel_l2(b["v2a_k"], b["ref_v2a_k"]) < 5e-3  # gathered: all tokens, all heads
+        assert _rel_l2(b["a2v_k"], b["ref_a2v_k"]) < 5e-3

@@ -118,13 +118,13 @@ def test_noalloc_without_split_equals_plain_entry():
 
 
 def test_noalloc_refuses_shapes_above_the_fixed_array():
-    """23 heads of 44 queries over 4608 keys: the partition splits every
-    query tile into 32 key ranges, 16.06 MiB of partial outputs.  The call is
+    """13 heads of 832 queries over 4608 keys: the partition splits every
+    query tile into 3 key ranges, 16.09 MiB of partial outputs.  The call is
     refused with TM_ERR_INVALID_ARGUMENT before any launch; out is untouched."""
     from taomate_b200 import _lib
     lib = _lib.load()
     torch.cuda.set_device(DEV)
-    H, D, Lq, Lk = 23, 128, 44, 4608
+    H, D, Lq, Lk = 13, 128, 832, 4608
     need = lib.tm_attention_workspace_bytes(1, Lq, H, D, Lk)
     assert need > FIXED_BYTES
     q, k, v = _inputs(11, H, D, Lq, Lk)
