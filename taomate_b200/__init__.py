@@ -9,6 +9,7 @@ Modules mirror the reference's layout for this path:
   kv_cache   -> LayerKVCache / KVCache / _cat_cache, plus the slot arena
   cache      -> taomate/inference/cache.py (segments, retain_streaming_context)
   parallel   -> taomate/runtime_support/parallel (Ulysses SP)
+  install    -> rebinds the reference's hot-path names to these (the drop-in)
 The compute runs in ``lib/libtaomate_b200.so`` (C ABI: include/taomate_b200.h).
 """
 
@@ -22,6 +23,7 @@ from .kv_cache import (ArenaKV, ArenaSpec, KVArena, KVCache, LayerKVCache, _cat_
 from .cache import (attach_segments, cache_segments, retain_streaming_context, retain_window)
 from . import block
 from .block import BlockWeights, block_forward_with_cache, fuse_block_weights
+from .install import install, uninstall
 
 __all__ = [
     "CausalRopeType", "apply_split_rotary_emb", "causal_precompute_freqs_cis",
@@ -32,4 +34,5 @@ __all__ = [
     "cat_cache_pair", "init_arena_cache",
     "attach_segments", "cache_segments", "retain_streaming_context", "retain_window",
     "block", "BlockWeights", "block_forward_with_cache", "fuse_block_weights",
+    "install", "uninstall",
 ]
