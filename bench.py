@@ -72,7 +72,8 @@ def parse():
     ap.add_argument("--qkv3", action="store_true",
                     help="three projection GEMMs per call instead of one over the fused weights")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["c4", "attention", "both"], default="both",
+    ap.add_argument("--segments", type=int, default=12, help="--workload c5: 5-block segments")
+    ap.add_argument("--workload", choices=["c4", "attention", "both", "c5"], default="both",
                     help="c4: the 48-block audio-video step (headline); attention: the video "
                          "self-attention step alone; both: c4 headline + attention as an extra key")
     ap.add_argument("--kernel-case", choices=["attention", "norm_rope", "kv_append"], default=None,
@@ -758,7 +759,97 @@ def c4_step(args, dev, rank, world, local, read_stream):
             "step_flops": step_flops,
             "step_tflops": step_flops / world / step_s / 1e12,
             "kv_cache_bytes_per_gpu": cache_bytes,
-            "realtime_factor": value / (25.0 / 8.0)}
+            # real time = 3 latent frames/s (24 fps video, 8x temporal compression)
+            "realtime_factor": value / 3.0}
+
+
+def c5_longform(args, dev, rank, world, local):
+    """a 60 s stream = 12 segments x 5 blocks (4-3-3-3-3
+    latent frames in the first window, then 3 per block; 181 latent frames),
+    as taomate/inference/runtime.py:569-634 drives it: a new prompt every
+    segment, whose K/V refresh re-prefills the retained blocks (sigma = 0
+    kv_cache_only forwards, runtime.py:386-470) from segment 1 on; no eviction
+    inside the first window, then sink + 2 newest after every block, and at
+    every window end.  Timed as a whole on the device (max over ranks),
+    including the eager first window, the graph capture and the refreshes."""
+    import torch
+    import torch.distributed as dist
+    from taomate_b200 import _lib
+    from taomate_b200.model import CausalModelWeights, StreamConfig, synthetic_conditioning
+    from taomate_b200.stream import StreamRunner, block_geometry
+
+    cfg = StreamConfig(layers=args.layers)
+    torch.manual_seed(0)
+    model = CausalModelWeights(cfg, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(9)
+    C = cfg.in_channels
+    segs, per = args.segments, 5
+    prompts = [synthetic_conditioning(cfg, 3, 25, dev, gen) for _ in range(segs)]
+    zero = {4: synthetic_conditioning(cfg, 4, 26, dev, gen),
+            3: synthetic_conditioning(cfg, 3, 25, dev, gen)}  # sigma = 0 rows by block size
+
+    def block_inputs(k):
+        F_, La, _, _ = block_geometry(k, cfg)
+        n = F_ * cfg.frame_tokens // world
+        v = torch.randn(1, n, C, device=dev, generator=gen).to(torch.bfloat16)
+        a = torch.randn(1, La, C, device=dev, generator=gen).to(torch.bfloat16)
+        return v, a, [synthetic_conditioning(cfg, F_, La, dev, gen) for _ in range(4)]
+
+    runner = StreamRunner(model, dev, sp=world, rank=rank, graphed=not args.eager,
+                          evict_from_block=per)
+    inputs = [block_inputs(k) for k in range(segs * per)]
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    frames = 0
+    peak_cache = 0
+    for sgi in range(segs):
+        runner.set_prompt(prompts[sgi].video_ctx, prompts[sgi].audio_ctx)
+        if sgi > 0:
+            conds = {int(sg["block_idx"]): zero[block_geometry(int(sg["block_idx"]), cfg)[0]]
+                     for sg in runner.cache.segments}
+            runner.refresh(conds)
+        for b in range(per):
+            k = sgi * per + b
+            runner.run_block(*inputs[k])
+            frames += block_geometry(k, cfg)[0]
+            peak_cache = max(peak_cache, live_cache_bytes(runner.cache))
+        runner.end_segment()
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    derr = _lib.device_error()
+    live = live_cache_bytes(runner.cache)
+    arena = sum(getattr(lay, f).arena.k.numel() * 2 * 2 for lay in runner.cache.layers
+                for f in ("video_self_k", "audio_self_k", "a2v_k", "v2a_k"))
+    if world > 1:
+        t = torch.tensor([ms, float(derr)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, derr = float(t[0].item()), int(t[1].item())
+    captured = runner.graph is not None
+    runner.release()
+    del model
+    torch.cuda.empty_cache()
+    video_s = (1 + 8 * (frames - 1)) / 24.0  # pixel frames at 24 fps (8x temporal compression)
+    return {"metric": "sustained latent frames/s over a 60 s stream (12 segments x 5 blocks)",
+            "value": frames / (ms / 1e3), "unit": "latent frames/s", "n_gpus": world,
+            "blocks": segs * per, "latent_frames": frames, "video_seconds": video_s,
+            "wall_ms": ms, "realtime_factor": video_s / (ms / 1e3),
+            "refreshes": runner.refreshes, "graph_captured": captured,
+            "kv_cache_bytes_per_gpu": live, "kv_cache_peak_bytes_per_gpu": peak_cache,
+            "kv_arena_bytes_per_gpu": arena, "clocks": clocks, "device_error": derr,
+            "config": {"workload": "C5: 60 s long-form stream", "segments": segs,
+                       "blocks_per_segment": per, "layers": args.layers,
+                       "prompt": "new 256-token text conditioning every segment (N(0, 1)), "
+                                 "K/V refresh of the retained blocks",
+                       "parallelism": f"ulysses sp{world} (video split, audio replicated)"
+                                      if world > 1 else "single gpu"}}
 
 
 COND_NAMES = ("video_ts", "audio_ts", "video_cross_ss", "video_cross_gate", "audio_cross_ss",
@@ -878,6 +969,15 @@ def run_ours(args):
         if not args.nccl_exchange:
             P.init_peer_exchange(1, Q_FRAMES * FRAME_TOKENS // world, HEADS, DIM_HEAD)
     read_stream = torch.cuda.Stream(dev)
+    if args.workload == "c5":
+        line = c5_longform(args, dev, rank, world, local)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            dist.barrier()
+            P.close_peer_exchange()
+            dist.destroy_process_group()
+        return
     parity = sp_parity(dev, rank, world) if world > 1 else None
     c4 = None if args.workload == "attention" else c4_step(args, dev, rank, world, local,
                                                            read_stream)

@@ -29,9 +29,11 @@ import torch.nn.functional as F
 
 from . import _lib
 from . import parallel as P
-from .cache import attach_segments, cache_segments, retain_streaming_context
+from .cache import (attach_segments, cache_segments, replace_modal_fields,
+                    retain_streaming_context)
 from .graphs import AttentionGraph, attention_spans, copy_bytes
-from .kv_cache import FIELD_PAIRS, KVCache, LayerKVCache, cat_cache_pair, last_chunk
+from .kv_cache import (FIELD_PAIRS, KVCache, LayerKVCache, arena_pair, cat_cache_pair,
+                       last_chunk)
 from .model import (CausalModelWeights, Conditioning, StreamConfig, arena_cache, model_forward,
                     rope_tables)
 from .rope import norm_rope
@@ -73,7 +75,8 @@ class StreamRunner:
         self.graph: Optional[AttentionGraph] = None
         self.text_graph: Optional[torch.cuda.CUDAGraph] = None
         self.ctx = None  # (video_ctx, audio_ctx) of the current prompt
-        self.launches = 0
+        self.latents = {}  # block_idx -> committed clean latents of the retained blocks
+        self.refreshes = 0
 
     # -- geometry -------------------------------------------------------------
     def local_tokens(self, frames: int) -> Tuple[int, int]:
@@ -84,9 +87,11 @@ class StreamRunner:
         return n, self.rank * n
 
     def steady(self) -> bool:
-        """The cache holds the sink block and two window blocks: every later
-        block sees the same number of key tiles per attention."""
-        return self.block >= max(3, self.evict_from_block + 3)
+        """The cache holds the sink block and two window blocks and eviction is
+        on: this and every later block see the same number of key tiles per
+        attention."""
+        return (self.block >= max(3, self.evict_from_block)
+                and len(cache_segments(self.cache)) == 3)
 
     # -- one forward ------------------------------------------------------------
     def _cond(self, c: Conditioning, pe) -> Conditioning:
@@ -121,16 +126,61 @@ class StreamRunner:
         latents (fresh tensors)."""
         if self.graphed and self.graph is None and self.steady():
             self._capture(video_latent, audio_latent, conds)
-        if self.graph is not None:
+        if self.graph is not None and self.steady():
             return self._replay_block(video_latent, audio_latent, conds)
         return self._eager_block(video_latent, audio_latent, conds)
+
+    def end_segment(self) -> None:
+        """The streaming eviction at a window boundary (runtime.py:634)."""
+        if len(cache_segments(self.cache)) > 3:
+            self.cache = retain_streaming_context(self.cache)
+        self._drop_latents()
+
+    def refresh(self, conds: dict) -> None:
+        """Re-prefill the prompt-sensitive K/V of the retained blocks with the
+        current prompt (``_refresh_conditioning_cache``, taomate/inference/
+        runtime.py:386-470): one sigma = 0 ``kv_cache_only`` forward per
+        retained segment, in order, over that block's committed clean
+        latents, each against the K/V rebuilt so far; then every field except
+        the video self-attention K/V is taken from the rebuilt cache (no data
+        moves).  The rebuilt rows go to free slots of the same arenas, so a
+        captured forward keeps reading them.  ``conds[block_idx]``: the
+        block's sigma = 0 conditioning rows."""
+        segs = cache_segments(self.cache)
+        if not segs:
+            raise RuntimeError("The retained cache has no block metadata.")
+        layers = []
+        for lay in self.cache.layers:
+            kw = {}
+            for kf, vf in FIELD_PAIRS:
+                kw[kf], kw[vf] = arena_pair(getattr(lay, kf).arena)
+            layers.append(LayerKVCache(**kw))
+        rebuilt = KVCache(layers=layers)
+        with torch.no_grad():
+            for seg in segs:
+                k = int(seg["block_idx"])
+                v, a = self.latents[k]
+                pe, off = self._pe(k)
+                _, _, rebuilt = model_forward(self.model, v, a, self._cond(conds[k], pe), rebuilt,
+                                              kv_cache_only=True, video_token_offset=off)
+                for lay in rebuilt.layers:
+                    for kf, _ in FIELD_PAIRS:
+                        getattr(lay, kf).entries()
+        self.cache = replace_modal_fields(self.cache, rebuilt)
+        self.refreshes += 1
+
+    def _drop_latents(self) -> None:
+        keep = {int(s["block_idx"]) for s in cache_segments(self.cache)}
+        for k in [k for k in self.latents if k not in keep]:
+            del self.latents[k]
 
     def _pe(self, k: int):
         F_, La, vs, as_ = block_geometry(k, self.cfg)
         n, off = self.local_tokens(F_)
         return rope_tables(self.cfg, F_, La, vs, as_, self.dev, slice(off, off + n)), off
 
-    def _commit(self, new_cache: KVCache) -> None:
+    def _commit(self, new_cache: KVCache, clean: Tuple[torch.Tensor, torch.Tensor]) -> None:
+        self.latents[self.block] = clean
         F_, La, _, _ = block_geometry(self.block, self.cfg)
         segs = cache_segments(self.cache) + [{"block_idx": self.block,
                                               "video_tokens": F_ * self.cfg.frame_tokens,
@@ -142,6 +192,7 @@ class StreamRunner:
         if self.block >= self.evict_from_block and len(segs) > 3:
             new_cache = retain_streaming_context(new_cache)
         self.cache = new_cache
+        self._drop_latents()
         self.block += 1
 
     def _eager_block(self, v, a, conds):
@@ -156,7 +207,7 @@ class StreamRunner:
                 x_a = torch.add(x_a, ao, alpha=dt)
             _, _, new = model_forward(self.model, x_v, x_a, self._cond(conds[3], pe), self.cache,
                                       kv_cache_only=True, video_token_offset=off)
-        self._commit(new)
+        self._commit(new, (x_v, x_a))
         return x_v, x_a
 
     # -- graph executor -------------------------------------------------------
@@ -251,8 +302,9 @@ class StreamRunner:
             for (kf, vf), (nk, nv) in zip(FIELD_PAIRS, chunks):
                 kw[kf], kw[vf] = cat_cache_pair(getattr(lay, kf), getattr(lay, vf), nk, nv)
             layers.append(LayerKVCache(**kw))
-        self._commit(KVCache(layers=layers))
-        return self._sv.clone(), self._sa.clone()
+        clean = (self._sv.clone(), self._sa.clone())
+        self._commit(KVCache(layers=layers), clean)
+        return clean
 
     def release(self):
         """Drop the captured graphs (before the process group goes away)."""
