@@ -3,6 +3,8 @@
 // vectors with consecutive threads on consecutive addresses of a row, so
 // reads and writes are fully coalesced; grids are sized in multiples of the
 // SM count.
+#include <algorithm>
+
 #include "common.cuh"
 #include "host_common.h"
 
@@ -23,15 +25,36 @@ struct RowsParams {
   int64_t vec_per_row;  // row_bytes / 16
 };
 
+// Each thread keeps kBatch independent 16-byte loads in flight before it
+// stores them (the loads of one batch index are coalesced across the warp);
+// a grid of about one wave then streams at HBM speed.  Index arithmetic in
+// 32 bits (a span's vectors are checked to fit on the host).
+constexpr int kBatch = 4;
+
 __global__ void __launch_bounds__(256) copy_rows_kernel(const __grid_constant__ RowsParams p) {
   const Span& s = p.spans[blockIdx.y];
-  const int64_t total = s.rows * p.vec_per_row;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = i / p.vec_per_row;
-    const int64_t v = i - r * p.vec_per_row;
-    const uint4 x = __ldg(reinterpret_cast<const uint4*>(s.src + r * s.srs) + v);
-    *(reinterpret_cast<uint4*>(s.dst + r * s.drs) + v) = x;
+  const uint32_t total = static_cast<uint32_t>(s.rows * p.vec_per_row);
+  const uint32_t vpr = static_cast<uint32_t>(p.vec_per_row);
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t base = blockIdx.x * blockDim.x + threadIdx.x; base < total;
+       base += kBatch * stride) {
+    uint4 x[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const uint32_t i = base + u * stride;
+      if (i < total) {
+        const uint32_t r = i / vpr, v = i - r * vpr;
+        x[u] = __ldg(reinterpret_cast<const uint4*>(s.src + static_cast<int64_t>(r) * s.srs) + v);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const uint32_t i = base + u * stride;
+      if (i < total) {
+        const uint32_t r = i / vpr, v = i - r * vpr;
+        *(reinterpret_cast<uint4*>(s.dst + static_cast<int64_t>(r) * s.drs) + v) = x[u];
+      }
+    }
   }
 }
 
@@ -108,12 +131,16 @@ extern "C" int tm_copy_rows(const tm_copy_span* spans, int n_spans, int64_t row_
     p.spans[i].srs = s.src_row_stride;
     p.spans[i].drs = s.dst_row_stride;
     const int64_t u = s.rows * p.vec_per_row;
+    if (u >= (int64_t(1) << 31))
+      return set_error(TM_ERR_INVALID_ARGUMENT, "copy_rows: span %d has 2^31 or more 16-byte "
+                       "vectors", i);
     if (u > max_units) max_units = u;
   }
   if (max_units == 0) return TM_OK;
   const int threads = 256;
-  int64_t bx = (max_units + threads - 1) / threads;
-  const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+  int64_t bx = (max_units + threads * kBatch - 1) / (threads * kBatch);
+  // about one wave of 8 blocks per SM over all spans
+  const int64_t cap = std::max<int64_t>(1, static_cast<int64_t>(num_sms()) * 8 / n_spans);
   if (bx > cap) bx = cap;
   dim3 grid(static_cast<unsigned>(bx), static_cast<unsigned>(n_spans));
   copy_rows_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(p);
