@@ -271,6 +271,74 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
+def cpu_breakdown():
+    """The CPU timings BASELINE lists beside the step, on the oracle port
+    (numpy fp32, all host BLAS threads), one warm-up then the minimum of 3:
+    attention_with_cache at C1 and C2 (projections included), the C2 RoPE
+    tables + split rotation of q and k, and one retain_streaming_context of a
+    48-layer cache at the production layout (every video and audio field)."""
+    import numpy as np
+    from oracle import ltx_oracle as O
+    f32 = np.float32
+    rng = np.random.default_rng(3)
+    out = {}
+
+    def best(fn):
+        fn()
+        ts = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return min(ts) * 1e3
+
+    def attn_case(hid, H, D, lq, lc, grid, start):
+        prm = {n: rng.standard_normal((hid, hid), dtype=f32) * f32(0.02)
+               for n in ("to_q_w", "to_k_w", "to_v_w", "to_out_w")}
+        for n in ("to_q_b", "to_k_b", "to_v_b", "to_out_b"):
+            prm[n] = rng.standard_normal(hid, dtype=f32) * f32(0.02)
+        prm["q_norm_w"] = prm["k_norm_w"] = np.ones(hid, f32)
+        x = rng.standard_normal((lq, hid), dtype=f32)
+        ck = rng.standard_normal((lc, H, D), dtype=f32)
+        cv = rng.standard_normal((lc, H, D), dtype=f32)
+        cos, sin = O.precompute_freqs_cis_split(grid, hid, start_frame=start, num_heads=H,
+                                                precision="f32")
+        pe = (cos.astype(f32), sin.astype(f32))
+        return lambda: O.attention_with_cache(x, prm, H, D, pe, ck, cv, dtype=f32)
+
+    out["attention_with_cache_c1_f32_ms"] = best(attn_case(256, 4, 64, 96, 576, (1, 8, 12), 6))
+    out["attention_with_cache_c2_f32_ms"] = best(
+        attn_case(HIDDEN, HEADS, DIM_HEAD, 1152, 3456, (3, 16, 24), 9))
+    xq = rng.standard_normal((1152, HIDDEN), dtype=f32)
+
+    def rope():
+        c, s_ = O.precompute_freqs_cis_split((3, 16, 24), HIDDEN, start_frame=9, num_heads=HEADS,
+                                             precision="f32")
+        c, s_ = c.astype(f32), s_.astype(f32)
+        O.apply_split_rotary_emb(xq, c, s_)
+        O.apply_split_rotary_emb(xq, c, s_)
+    out["rope_tables_and_rotate_qk_c2_ms"] = best(rope)
+    segs = [{"block_idx": 0, "video_tokens": 1536, "audio_tokens": 26}] + \
+        [{"block_idx": i, "video_tokens": 1152, "audio_tokens": 25} for i in (1, 2, 3)]
+    layer = {"video": rng.standard_normal((4992, 32, 128), dtype=f32).astype(np.float16),
+             "v2a": rng.standard_normal((4992, 32, 64), dtype=f32).astype(np.float16),
+             "audio": rng.standard_normal((101, 32, 64), dtype=f32).astype(np.float16)}
+
+    def retain():
+        keep = O.retain_indices(segs)
+        vs, as_ = O.slice_spans(segs, keep)
+        for _ in range(48):
+            for _kv in range(2):  # K and V of each pair
+                O.slice_tensor(layer["video"], vs, axis=0)
+                O.slice_tensor(layer["v2a"], vs, axis=0)
+                O.slice_tensor(layer["audio"], as_, axis=0)
+                O.slice_tensor(layer["audio"], as_, axis=0)
+    out["retain_streaming_context_48_layers_ms"] = best(retain)
+    out["note"] = ("numpy restatement; the reference's own bf16 CPU path is not timed (numpy has "
+                   "no bf16; 16-bit storage is used for the retained cache rows)")
+    return out
+
+
 def run_reference(args):
     """The reference's CPU arm: the numpy restatement of the reference block
     (the reference itself is pure PyTorch and its source tree does not travel
@@ -298,6 +366,7 @@ def run_reference(args):
                                    f"restatement of block_forward_with_cache, mean {t:.3f} s"},
         "e2e": {"value": value, "unit": "latent frames/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        "cpu_breakdown": cpu_breakdown(),
     }
     print(json.dumps(line), flush=True)
 
