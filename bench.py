@@ -785,12 +785,17 @@ def c4_step(args, dev, rank, world, local, read_stream):
             h2d = sum(x.numel() * x.element_size() for x in host[0])
             d2h = sum(x.numel() * x.element_size() for x in outs[0])
         cache_bytes = live_cache_bytes(runner.cache)
+        HOST_MS.clear()
+        if runner.host_blocks:
+            HOST_MS.update({k: v / runner.host_blocks for k, v in runner.host_ms.items()})
         runner.release()
         return ms, launches, clocks, h2d, d2h, cache_bytes
 
     DEVICE_ERRORS = []
+    HOST_MS = {}
     warm = max(args.warmup, 3)
     ms, launches, clocks, _, _, cache_bytes = timed(args.steps, warm)
+    host_ms = dict(HOST_MS)  # host time per replayed block of the headline pass, by phase
     value = 3.0 * args.steps / (ms / 1e3)
     timed(max(2, min(args.steps, 5)), warm, sections=True)
     sections = TIMER.summary()
@@ -825,7 +830,7 @@ def c4_step(args, dev, rank, world, local, read_stream):
     return {"value": value, "ms_per_step": ms / args.steps, "e2e": e2e, "roofline": roof,
             "gpu_launches": launches, "clocks": clocks, "device_error": max(DEVICE_ERRORS),
             "sections_ms_per_call": {k: v["mean_ms"] for k, v in sections.items()},
-            "step_flops": step_flops,
+            "step_flops": step_flops, "host_ms_per_block": host_ms,
             "step_tflops": step_flops / world / step_s / 1e12,
             "kv_cache_bytes_per_gpu": cache_bytes,
             # real time = 3 latent frames/s (24 fps video, 8x temporal compression)
@@ -1083,7 +1088,7 @@ def run_ours(args):
         }
         if c4 is not None:
             line.update({k: c4[k] for k in ("step_flops", "step_tflops", "kv_cache_bytes_per_gpu",
-                                            "realtime_factor")})
+                                            "realtime_factor", "host_ms_per_block")})
             if att is not None:
                 line["attention_step"] = {k: att[k] for k in ("value", "ms_per_step", "roofline",
                                                               "sections_ms_per_call", "config")}

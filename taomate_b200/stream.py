@@ -21,6 +21,7 @@ K/V cache is on, which keeps them per prompt).
 
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass, fields
 from typing import List, Optional, Sequence, Tuple
 
@@ -33,7 +34,7 @@ from .cache import (attach_segments, cache_segments, replace_modal_fields,
                     retain_streaming_context)
 from .graphs import AttentionGraph, attention_spans, copy_bytes
 from .kv_cache import (FIELD_PAIRS, KVCache, LayerKVCache, arena_pair, cat_cache_pair,
-                       last_chunk)
+                       flush_many, last_chunk)
 from .model import (CausalModelWeights, Conditioning, StreamConfig, arena_cache, model_forward,
                     rope_tables)
 from .rope import norm_rope
@@ -77,6 +78,8 @@ class StreamRunner:
         self.ctx = None  # (video_ctx, audio_ctx) of the current prompt
         self.latents = {}  # block_idx -> committed clean latents of the retained blocks
         self.refreshes = 0
+        self.host_ms = {}  # host time of the replayed blocks, by phase
+        self.host_blocks = 0
 
     # -- geometry -------------------------------------------------------------
     def local_tokens(self, frames: int) -> Tuple[int, int]:
@@ -186,9 +189,8 @@ class StreamRunner:
                                               "video_tokens": F_ * self.cfg.frame_tokens,
                                               "audio_tokens": La}]
         attach_segments(new_cache, segs)
-        for lay in new_cache.layers:  # copy the pending chunks into their slots now
-            for kf, vf in FIELD_PAIRS:
-                getattr(lay, kf).entries()
+        # copy the pending chunks into their slots now, in a few batched launches
+        flush_many([getattr(lay, kf) for lay in new_cache.layers for kf, _ in FIELD_PAIRS])
         if self.block >= self.evict_from_block and len(segs) > 3:
             new_cache = retain_streaming_context(new_cache)
         self.cache = new_cache
@@ -283,11 +285,13 @@ class StreamRunner:
                        self.dev)
 
     def _replay_block(self, v, a, conds):
+        t0 = time.perf_counter()
         pe, off = self._pe(self.block)
         self._load(self._static_pe, [t for pair in pe for t in pair])
         self._load([self._sv, self._sa], [v, a])
         self.text_graph.replay()
         spans = self._spans(self.cache)
+        t1 = time.perf_counter()
         for fwd in range(4):
             self._load(self._static_cond, [getattr(conds[fwd], n) for n in COND_FIELDS])
             self.graph.replay(spans if fwd == 0 else None)
@@ -295,6 +299,7 @@ class StreamRunner:
                 dt = SIGMAS[fwd + 1] - SIGMAS[fwd]
                 self._sv.add_(self._out_v, alpha=dt)
                 self._sa.add_(self._out_a, alpha=dt)
+        t2 = time.perf_counter()
         # commit: this block's K/V (the fourth replay's) appended to the cache
         layers = []
         for lay, chunks in zip(self.cache.layers, self._chunks):
@@ -304,6 +309,10 @@ class StreamRunner:
             layers.append(LayerKVCache(**kw))
         clean = (self._sv.clone(), self._sa.clone())
         self._commit(KVCache(layers=layers), clean)
+        t3 = time.perf_counter()
+        for k, dt in (("prepare", t1 - t0), ("replays", t2 - t1), ("commit_evict", t3 - t2)):
+            self.host_ms[k] = self.host_ms.get(k, 0.0) + dt * 1e3
+        self.host_blocks += 1
         return clean
 
     def release(self):
