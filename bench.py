@@ -76,7 +76,8 @@ def parse():
     ap.add_argument("--workload", choices=["c4", "attention", "both", "c5"], default="both",
                     help="c4: the 48-block audio-video step (headline); attention: the video "
                          "self-attention step alone; both: c4 headline + attention as an extra key")
-    ap.add_argument("--kernel-case", choices=["attention", "norm_rope", "kv_append"], default=None,
+    ap.add_argument("--kernel-case", choices=["attention", "norm_rope", "kv_append",
+                                              "residual_norm"], default=None,
                     help="time one kernel in isolation at C2 shapes (profiling target)")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--heads", type=int, default=None,
@@ -1147,6 +1148,17 @@ def run_kernel_case(args):
                 arena._ref(slot, -1)
 
         work, unit = 4.0 * Lq * HEADS * DIM_HEAD * 2 / 1e9, "GB/s"
+    elif args.kernel_case == "residual_norm":
+        # the cross-modal boundary of the C4 block: r = x + y * gate stored, then two
+        # modulations of rms_norm(r) (A2V and V2A inputs); AdaLN rows per frame
+        from taomate_b200.block import AdaParams, residual_norm
+        x, y = rnd(1, Lq, HIDDEN), rnd(1, Lq, HIDDEN)
+        o1, o2 = torch.empty_like(x), torch.empty_like(x)
+        table = rnd(6, HIDDEN) * 0.1
+        ts = rnd(1, Q_FRAMES, 6 * HIDDEN) * 0.1
+        prm = AdaParams(table, ts, Lq, 6, HIDDEN, FRAME_TOKENS, 0)
+        fn = lambda: residual_norm(x, y, prm, 2, x, [(o1, prm, 1, 0), (o2, prm, 4, 3)])
+        work, unit = 5 * Lq * HIDDEN * 2 / 1e9, "GB/s"  # x, y read; x, o1, o2 written
     else:
         xq, xk = rnd(1, Lq, HIDDEN), rnd(1, Lq, HIDDEN)
         w = torch.ones(HIDDEN, device=dev, dtype=torch.bfloat16)
