@@ -317,8 +317,20 @@ TM_API int64_t tm_attention_workspace_bytes(int B, int Lq, int H, int D, int64_t
  *                    elements): each output row of head h is multiplied by
  *                    2 * sigmoid(logit) before it is stored — the per-head gate
  *                    of kv_cache.py:1691-1697 fused into the epilogue
+ *   parts, _bytes    export partial results instead of storing `out` (which
+ *                    may then be NULL; placement, gate and workspace are
+ *                    ignored): the visible keys are divided into part_splits
+ *                    ranges, and for each range the normalised fp32 output
+ *                    and its (max * log2 scale, sum) go to `parts` in the
+ *                    tm_attention_partial_bytes layout.  Several GPUs that
+ *                    each attend over their own share of the keys gather
+ *                    their parts and merge them with tm_attention_combine.
+ *   part_splits      key ranges of an export (1 .. visible key tiles);
+ *                    tm_attention_partial_splits suggests one
  * Replaces the attention + head->seq all-to-all of attention_with_cache
- * (kv_cache.py:1531-1538, all_to_all.py:154-173).
+ * (kv_cache.py:1531-1538, all_to_all.py:154-173); with `parts`, the
+ * attention + both exchanges of V2A under sequence parallelism
+ * (kv_cache.py:1432-1462, 1535-1538), where the keys are split by rank.
  */
 typedef struct {
   const void* device_tiles;
@@ -330,7 +342,40 @@ typedef struct {
   const void* gate_logits;
   int64_t gate_batch_stride;
   int64_t gate_row_stride;
+  void* parts;
+  int64_t parts_bytes;
+  int32_t part_splits;
+  int32_t reserved;
 } tm_attention_ext;
+
+/*
+ * Bytes of one export of tm_attention_fwd_ext `parts` with `splits` key
+ * ranges: [splits][B][Lq][H][D] fp32 normalised outputs, then, at the next
+ * 256-byte boundary, [splits][B][Lq][H] float2 (max * log2 scale, sum).
+ */
+TM_API int64_t tm_attention_partial_bytes(int B, int Lq, int H, int D, int splits);
+
+/*
+ * Key ranges for an export over `visible_keys` keys that keep every SM busy
+ * (the kernel's own work-partition cost model), >= 1.
+ */
+TM_API int tm_attention_partial_splits(int B, int Lq, int H, int D, int64_t visible_keys);
+
+/*
+ * Merge n_groups exports of `splits` key ranges each (group g at byte offset
+ * g * group_bytes from `parts`, 16-byte aligned, group_bytes >=
+ * tm_attention_partial_bytes) into out [B, Lq, H, D] bf16 (strides in
+ * elements, multiples of 8), as one softmax over all their keys; with
+ * gate_logits, each row of head h is multiplied by 2 * sigmoid(logit) as in
+ * tm_attention_fwd_ext.  The merge order is fixed (group-major), so GPUs
+ * that merge the same gathered bytes store the same bits.  Reference
+ * interface: the V2A output of kv_cache.py:1531-1538 after its head->seq
+ * exchange.
+ */
+TM_API int tm_attention_combine(const void* parts, int n_groups, int64_t group_bytes, int splits,
+                     int B, int Lq, int H, int D, void* out, int64_t out_batch_stride,
+                     int64_t out_row_stride, const void* gate_logits, int64_t gate_batch_stride,
+                     int64_t gate_row_stride, void* stream);
 
 TM_API int tm_attention_fwd_ext(const void* q, int64_t q_batch_stride, int64_t q_row_stride,
                      const void* k_cache, const void* v_cache, int64_t cache_batch_stride,

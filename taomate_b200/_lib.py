@@ -47,7 +47,8 @@ class AttentionExt(ctypes.Structure):
     _fields_ = [("device_tiles", c_vp), ("workspace", c_vp), ("workspace_bytes", c_i64),
                 ("rows_per_rank", ctypes.c_int32), ("head_base", ctypes.c_int32),
                 ("out_delta", c_i64 * 8), ("gate_logits", c_vp), ("gate_batch_stride", c_i64),
-                ("gate_row_stride", c_i64)]
+                ("gate_row_stride", c_i64), ("parts", c_vp), ("parts_bytes", c_i64),
+                ("part_splits", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 class CopySpan(ctypes.Structure):
@@ -99,6 +100,11 @@ _SIGS = {
                                            ctypes.c_int, ctypes.c_float, c_vp, c_i64, c_vp]),
     "tm_attention_workspace_bytes": (c_i64, [ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                              ctypes.c_int, c_i64]),
+    "tm_attention_partial_bytes": (c_i64, [ctypes.c_int] * 5),
+    "tm_attention_partial_splits": (ctypes.c_int, [ctypes.c_int] * 4 + [c_i64]),
+    "tm_attention_combine": (ctypes.c_int, [c_vp, ctypes.c_int, c_i64, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, ctypes.c_int, ctypes.c_int, c_vp, c_i64,
+                                            c_i64, c_vp, c_i64, c_i64, c_vp]),
     "tm_attention_tiles": (ctypes.c_int, [ctypes.POINTER(KVSpan), ctypes.c_int, c_i64, c_i64,
                                           c_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "tm_attention_fwd_dev_tiles": (ctypes.c_int, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64,

@@ -46,7 +46,8 @@ def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tens
                     cache_spans: Sequence[Tuple[int, int]], new_k: Optional[Tensor],
                     new_v: Optional[Tensor], new_rows: int, scale: Optional[float] = None,
                     out: Optional[Tensor] = None, peer=None,
-                    gate_logits: Optional[Tensor] = None) -> Tensor:
+                    gate_logits: Optional[Tensor] = None, parts: Optional[Tensor] = None,
+                    part_splits: int = 1) -> Tensor:
     """``softmax(q K^T * scale) V`` with the keys of ``cache_spans`` (row ranges
     of ``cache_k/v``) followed by the first ``new_rows`` rows of ``new_k/v``.
     All tensors ``[B, L, H, D]`` bf16 with contiguous heads.
@@ -56,14 +57,29 @@ def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tens
     head->seq exchange); the caller then runs ``peer.exchange(1)`` and reads
     ``peer.out``, which is also what this returns.  ``gate_logits``
     (``[B, Lq, H]`` bf16) multiplies each output row of head h by
-    ``2 * sigmoid(logit)`` in the kernel's epilogue."""
+    ``2 * sigmoid(logit)`` in the kernel's epilogue.
+
+    With ``parts`` (a uint8 tensor of :func:`partial_bytes`) the call
+    stores no output: the keys are divided into ``part_splits`` ranges and
+    each range's normalised fp32 output and (max, sum) go to ``parts``, for
+    :func:`combine_partials` to merge with other GPUs' parts; returns
+    ``parts``."""
     dev = _lib.require_cuda(q, cache_k, new_k)
     B, Lq, H, D = (int(v) for v in q.shape)
     if q.dtype != torch.bfloat16:
         raise TypeError(f"expected bfloat16, got {q.dtype}")
     qbs, qrs = _row_strides(q, H, D)
     ext = _lib.AttentionExt()
-    if peer is not None:
+    if parts is not None:
+        if peer is not None or gate_logits is not None or out is not None:
+            raise ValueError("an export of partial results takes no output, peer or gate")
+        need = partial_bytes(B, Lq, H, D, part_splits)
+        if parts.dtype != torch.uint8 or parts.numel() < need or not parts.is_contiguous():
+            raise ValueError(f"parts must be a contiguous uint8 tensor of {need} bytes")
+        ext.parts, ext.parts_bytes, ext.part_splits = parts.data_ptr(), parts.numel(), part_splits
+        out = parts
+        obs, ors = 0, H * D
+    elif peer is not None:
         if Lq != peer.sp * peer.S_loc or H != peer.Hl or D != peer.D or B != peer.B:
             raise ValueError("attention output does not match the peer exchange's shapes")
         out = peer.out
@@ -105,7 +121,7 @@ def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tens
         nrows = int(new_k.shape[1])
     lib = _lib.load()
     keys = sum(n for (_, _, n) in spans)
-    ws_bytes = _workspace_bytes(lib, dev, B, Lq, H, D, keys)
+    ws_bytes = 0 if parts is not None else _workspace_bytes(lib, dev, B, Lq, H, D, keys)
     # the key-range split's partial outputs live in a torch-owned workspace
     if ws_bytes:
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
@@ -126,6 +142,50 @@ def flash_attention(q: Tensor, cache_k: Optional[Tensor], cache_v: Optional[Tens
             float(scale) if scale is not None else 0.0, ctypes.byref(ext),
             _lib.stream_ptr(dev)), "attention")
         _lib.launched(2 if ws_bytes else 1)  # + the merge kernel of a key-range split
+    return out
+
+
+def partial_bytes(B: int, Lq: int, H: int, D: int, splits: int) -> int:
+    """Bytes of one export of partial results (``flash_attention(parts=)``)
+    with ``splits`` key ranges, a multiple of 16."""
+    n = int(_lib.load().tm_attention_partial_bytes(B, Lq, H, D, splits))
+    if n <= 0:
+        raise ValueError(f"no partial layout for B={B} Lq={Lq} H={H} D={D} splits={splits}")
+    return (n + 15) // 16 * 16
+
+
+def partial_splits(B: int, Lq: int, H: int, D: int, keys: int) -> int:
+    """Key ranges per query tile that keep the SMs busy for an export over
+    ``keys`` keys (the kernel's work-partition cost model)."""
+    return int(_lib.load().tm_attention_partial_splits(B, Lq, H, D, keys))
+
+
+def combine_partials(parts: Tensor, n_groups: int, group_bytes: int, splits: int, B: int,
+                     Lq: int, H: int, D: int, out: Optional[Tensor] = None,
+                     gate_logits: Optional[Tensor] = None) -> Tensor:
+    """Merge ``n_groups`` exports of ``splits`` key ranges each (group g at
+    byte ``g * group_bytes`` of ``parts``: one group per GPU after an
+    all-gather) into ``out [B, Lq, H, D]`` bf16, one softmax over all their
+    keys; ``gate_logits`` as in :func:`flash_attention`.  The merge order is
+    fixed, so every GPU merging the same bytes gets the same bits."""
+    dev = _lib.require_cuda(parts)
+    if parts.dtype != torch.uint8 or not parts.is_contiguous() or \
+            parts.numel() < (n_groups - 1) * group_bytes + partial_bytes(B, Lq, H, D, splits):
+        raise ValueError("parts: a contiguous uint8 tensor holding every group")
+    if out is None:
+        out = torch.empty(B, Lq, H, D, device=dev, dtype=torch.bfloat16)
+    obs, ors = _row_strides(out, H, D)
+    gp, gbs, grs = None, 0, 0
+    if gate_logits is not None:
+        if gate_logits.dtype != torch.bfloat16 or gate_logits.shape != (B, Lq, H) or \
+                gate_logits.stride(2) != 1:
+            raise ValueError("gate logits must be [B, Lq, H] bf16 with unit head stride")
+        gp, gbs, grs = gate_logits.data_ptr(), gate_logits.stride(0), gate_logits.stride(1)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().tm_attention_combine(
+            parts.data_ptr(), n_groups, group_bytes, splits, B, Lq, H, D, out.data_ptr(), obs,
+            ors, gp, gbs, grs, _lib.stream_ptr(dev)), "attention combine")
+        _lib.launched()
     return out
 
 

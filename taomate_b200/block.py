@@ -166,52 +166,70 @@ def feed_forward(ff, x: Tensor) -> Tensor:
     return F.linear(h, out.weight, out.bias)
 
 
-def video_to_audio_gathered(attn, ax_v2a: Tensor, vx_v2a: Tensor, audio_cross_pe, video_cross_pe,
-                            cached_k, cached_v, video_real_len: Optional[int] = None):
+def video_to_audio_split_keys(attn, ax_v2a: Tensor, vx_v2a: Tensor, audio_cross_pe,
+                              video_cross_pe, cached_k, cached_v,
+                              video_real_len: Optional[int] = None):
     """V2A attention (audio queries over video keys) when the audio stream is
     replicated on every rank and the video stream is split by sequence.
 
     The reference moves Q, K and V seq->head and the output head->seq
     (kv_cache.py:1432-1462, 1535-1538) over audio tokens padded to the rank
-    count.  Here each rank projects its own video tokens' K/V (norm + cross
-    RoPE fused, K and V interleaved per token) and one all-gather gives every
-    rank the chunk's K/V for all heads; the 25 audio queries then attend over
-    the cached and new video keys for all heads on every rank, so the output
-    is already replicated.  Cached and returned K/V hold all heads."""
+    count, so every rank attends its heads over all video keys.  Here the
+    keys stay where they were made: each rank projects its own video tokens'
+    K/V (norm + cross RoPE fused) and attends the 25 audio queries, all heads,
+    over its own cached and new video keys, exporting per key range the
+    normalised fp32 output and its (max, sum) (tm_attention_fwd_ext with
+    parts, ~0.2 MB); one all-gather of those parts, and every rank merges all
+    ranks' parts in the same order (tm_attention_combine, the per-head gate
+    fused), so the output is the same softmax over all keys and the same bits
+    on every rank.  The V2A cache of each rank holds its own video tokens
+    (all heads); this call returns those new K/V."""
     import torch.distributed as dist
-    G, grp = P.get_sp_world_size(), P.get_sp_group()
+    from .attention import combine_partials, partial_bytes, partial_splits
+    G, grp, r = P.get_sp_world_size(), P.get_sp_group(), P.get_sp_rank()
     H, D = int(attn.heads), int(attn.dim_head)
-    B, Lloc = int(vx_v2a.shape[0]), int(vx_v2a.shape[1])
+    B, Lloc, La = int(vx_v2a.shape[0]), int(vx_v2a.shape[1]), int(ax_v2a.shape[1])
     if B != 1:
-        raise NotImplementedError("the gathered V2A path takes batch 1")
+        raise NotImplementedError("the split-key V2A path takes batch 1")
     eps = _norm_eps(attn.q_norm)
     with section("video_to_audio.qkv_proj_norm"):
         q = F.linear(ax_v2a, attn.to_q.weight, attn.to_q.bias)
         k = F.linear(vx_v2a, attn.to_k.weight, attn.to_k.bias)
-        v = F.linear(vx_v2a, attn.to_v.weight, attn.to_v.bias)
+        v = F.linear(vx_v2a, attn.to_v.weight, attn.to_v.bias).view(B, Lloc, H, D)
     with section("video_to_audio.rope_reshape"):
         (q,) = norm_rope([q], [attn.q_norm.weight], [audio_cross_pe], H, D, eps)
-        send = norm_rope([k, v], [attn.k_norm.weight, None], [video_cross_pe, None], H, D, eps,
-                         packed=True)  # [1, 1, Lloc, 2, H, D]
-    recv = torch.empty((G,) + tuple(send.shape[1:]), device=send.device, dtype=send.dtype)
-    with section("video_to_audio.all_gather"):
-        dist.all_gather_into_tensor(recv, send, group=grp)
-    flat = recv.view(G * Lloc, 2, H, D)
-    k_full, v_full = flat[:, 0].unsqueeze(0), flat[:, 1].unsqueeze(0)
-    n = G * Lloc
-    if video_real_len is not None and video_real_len < n:
-        n = int(video_real_len)
-        k_full, v_full = k_full[:, :n], v_full[:, :n]
+        (k,) = norm_rope([k], [attn.k_norm.weight], [video_cross_pe], H, D, eps)
+    n = Lloc  # this rank's real video rows of the chunk
+    if video_real_len is not None:
+        n = max(0, min(Lloc, int(video_real_len) - r * Lloc))
+    k, v = k[:, :n], v[:, :n]
     ck, cv, spans = _cache_source(cached_k, cached_v)
+    cached = sum(int(rows) for _, rows in spans)
+    # the same number of key ranges on every rank (ranks hold equal cache rows)
+    splits = partial_splits(B, La, H, D, cached + Lloc)
+    pb = partial_bytes(B, La, H, D, splits)
+    gathered = torch.empty(G * pb, dtype=torch.uint8, device=q.device)
+    own = gathered[r * pb:(r + 1) * pb]
     with section("video_to_audio.sdpa"):
-        out = flash_attention(q, ck, cv, spans, k_full, v_full, n)
-    with section("video_to_audio.out_proj"):
-        out = out.reshape(B, -1, H * D)
+        if cached + n == 0:
+            # no keys on this rank: a part of weight zero, (max, sum) = (-inf, 0)
+            rows = splits * B * La * H
+            off = (rows * D * 4 + 255) // 256 * 256
+            own.zero_()
+            ml = own[off:off + rows * 8].view(torch.float32).view(rows, 2)
+            ml[:, 0] = float("-inf")
+        else:
+            flash_attention(q, ck, cv, spans, k, v, n, parts=own, part_splits=splits)
+    with section("video_to_audio.all_gather"):
+        dist.all_gather_into_tensor(gathered, own, group=grp)
+    with section("video_to_audio.combine"):
+        glog = None
         if getattr(attn, "to_gate_logits", None) is not None:
-            gates = 2.0 * torch.sigmoid(attn.to_gate_logits(ax_v2a))
-            out = (out.view(B, -1, H, D) * gates.unsqueeze(-1)).view(B, -1, H * D)
-        out = attn.to_out(out)
-    return out, k_full, v_full
+            glog = attn.to_gate_logits(ax_v2a)
+        out = combine_partials(gathered, G, pb, splits, B, La, H, D, gate_logits=glog)
+    with section("video_to_audio.out_proj"):
+        out = attn.to_out(out.view(B, La, H * D))
+    return out, k, v
 
 
 _AUDIO_STREAMS = {}
@@ -298,9 +316,10 @@ def block_forward_with_cache(
     (``video_token_offset`` = its first token).  The audio stream is split
     the same way (the reference's layout) unless ``audio_replicated``: then
     every rank holds all audio tokens, the audio sublayers and A2V run
-    locally with all heads, V2A gathers the chunk's video K/V once
-    (:func:`video_to_audio_gathered`), and the audio, A2V and V2A caches hold
-    all heads.  ``overlap_audio`` runs the audio chain on a second stream
+    locally with all heads, V2A attends over each rank's own video keys and
+    merges the ranks' partial results (:func:`video_to_audio_split_keys`);
+    the audio and A2V caches hold all heads, the V2A cache this rank's video
+    tokens with all heads.  ``overlap_audio`` runs the audio chain on a second stream
     beside the video chain (same kernels, same results)."""
     if pyramid_policy is not None:
         raise NotImplementedError("pyramid KV selection is disabled in every shipped config")
@@ -415,7 +434,7 @@ def block_forward_with_cache(
         # audio chain: V2A, gated residual + FFN input (slice 3:6), FFN
         with torch.cuda.stream(side):
             if audio_local:
-                v2a_out, new_v2a_k, new_v2a_v = video_to_audio_gathered(
+                v2a_out, new_v2a_k, new_v2a_v = video_to_audio_split_keys(
                     block.video_to_audio_attn, ax_v2a, vx_v2a, audio_cross_pe, video_cross_pe,
                     layer_cache.v2a_k, layer_cache.v2a_v, video_real_len)
             else:

@@ -106,20 +106,41 @@ def _slice_pair(k, v, spans: List[Tuple[int, int]]):
     return _slice_tensor(k, spans), _slice_tensor(v, spans)
 
 
+def _field_spans(spans: List[Tuple[int, int]], tokens: int, field) -> List[Tuple[int, int]]:
+    """Token spans as row spans of a cache field that holds every token
+    (rows == tokens) or one rank's equal share of each segment's tokens
+    (tokens / rows rows per token: the split-key V2A cache under sequence
+    parallelism)."""
+    if field is None:
+        return spans
+    rows = int(field.shape[1])
+    if rows == tokens:
+        return spans
+    if rows == 0 or tokens % rows:
+        raise ValueError(f"a cache field of {rows} rows does not hold shares of {tokens} tokens")
+    f = tokens // rows
+    if any(s % f or e % f for s, e in spans):
+        raise ValueError(f"segment boundaries do not split over {f} ranks")
+    return [(s // f, e // f) for s, e in spans]
+
+
 def _slice_cache(cache: KVCache, indices: List[int]) -> KVCache:
     """Keep the segments ``indices`` of every layer field (cache.py:34-56):
     video spans slice ``video_self_*`` and ``v2a_*``, audio spans slice
-    ``audio_self_*`` and ``a2v_*``."""
+    ``audio_self_*`` and ``a2v_*`` (a V2A cache holding one rank's share of
+    the video tokens is sliced by the same share of each span)."""
     segments = cache_segments(cache)
     offsets = _segment_offsets(segments)
     video_spans = [(offsets[i][0], offsets[i][1]) for i in indices]
     audio_spans = [(offsets[i][2], offsets[i][3]) for i in indices]
+    video_tokens = offsets[-1][1] if offsets else 0
     layers = []
     for layer in cache.layers:
         vk, vv = _slice_pair(layer.video_self_k, layer.video_self_v, video_spans)
         ak, av = _slice_pair(layer.audio_self_k, layer.audio_self_v, audio_spans)
         a2k, a2v = _slice_pair(layer.a2v_k, layer.a2v_v, audio_spans)
-        v2k, v2v = _slice_pair(layer.v2a_k, layer.v2a_v, video_spans)
+        v2k, v2v = _slice_pair(layer.v2a_k, layer.v2a_v,
+                               _field_spans(video_spans, video_tokens, layer.v2a_k))
         layers.append(LayerKVCache(video_self_k=vk, video_self_v=vv, audio_self_k=ak,
                                    audio_self_v=av, a2v_k=a2k, a2v_v=a2v, v2a_k=v2k, v2a_v=v2v))
     return attach_segments(KVCache(layers=layers), [segments[i] for i in indices])

@@ -15,6 +15,10 @@
 // query tile, and with a workspace the key tiles are further divided into
 // kv_splits ranges, one CTA each; those CTAs write normalised fp32 partial
 // outputs with their (max, sum), and a combine kernel merges the ranges.
+// The same partial outputs can be exported instead (tm_attention_fwd_ext with
+// `parts`): each of several GPUs attends over its own share of the keys, the
+// partials are gathered, and tm_attention_combine merges them (V2A under
+// sequence parallelism: 25 audio queries over keys split by rank).
 //
 // Shared memory: the query tile(s) (TMA, 128-byte swizzle), a 4-stage K ring
 // and a 5-stage V ring of 64-key tiles.  TMEM (512 columns): S_l at 64 l
@@ -77,6 +81,7 @@ struct __align__(64) Params {
   const int2* tiles_dev;  // non-null: read the key-tile list from device memory (graph replay)
   int mode;               // 0: pair CTAs (+ one split CTA for an odd tile); 1: split CTAs only
   int kv_splits;          // mode 1: key-tile ranges per query tile
+  int partial_only;       // part_o / part_ml belong to the caller: no combine pass
   CUtensorMap tm_q;
   CUtensorMap tm_k[2];  // [TM_KV_SOURCE_CACHE], [TM_KV_SOURCE_NEW]
   CUtensorMap tm_v[2];
@@ -506,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         s1 = c1 * inv;
       }
       const uint32_t tO1 = t_lane + C::kOCol + D;
-      if (kvs > 1) {
+      if (p.part_o) {
         // Normalised partial output of this key range, and its (max, sum).
         // The TMEM loads are warp-collective: every lane runs them, rows past
         // Lq only skip the stores.
@@ -638,9 +643,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   }
 }
 
-// Merge of the kv_splits key ranges: one warp per (batch, query row, head);
-// out = sum_s w_s O_s / sum_s w_s with w_s = l_s 2^(m_s - max_s m_s), O_s the
-// range's normalised output.
+// Merge of partial outputs: one warp per (batch, query row, head); out =
+// sum_s w_s O_s / sum_s w_s with w_s = l_s 2^(m_s - max_s m_s), O_s a key
+// range's normalised output.  The partials come in n_groups groups of kvs
+// (group g at byte offset g * group_bytes from part_o / part_ml: one group per
+// GPU of a gathered exchange), merged in group-major order, so every GPU that
+// merges the same gathered bytes stores the same bits.
 struct OutPlace {
   __nv_bfloat16* out;
   int64_t out_bs, out_rs;
@@ -653,6 +661,7 @@ struct OutPlace {
 template <int D>
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ part_o,
                                                       const float2* __restrict__ part_ml, int kvs,
+                                                      int n_groups, int64_t group_bytes,
                                                       int B, int Lq, int H,
                                                       const __grid_constant__ OutPlace op) {
   constexpr int kPer = D / 32;  // columns per lane
@@ -663,17 +672,27 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
   const int h = static_cast<int>(w % H);
   const int qi = static_cast<int>((w / H) % Lq);
   const int b = static_cast<int>(w / (static_cast<int64_t>(H) * Lq));
+  const int np = n_groups * kvs;
+  auto ml_of = [&](int i) {
+    const int g = i / kvs, s = i - g * kvs;
+    return reinterpret_cast<const float2*>(reinterpret_cast<const char*>(part_ml) +
+                                           g * group_bytes)[s * total + w];
+  };
   float mmax = -INFINITY;
-  for (int s = 0; s < kvs; ++s) mmax = fmaxf(mmax, part_ml[s * total + w].x);
+  for (int i = 0; i < np; ++i) mmax = fmaxf(mmax, ml_of(i).x);
   float acc[kPer];
 #pragma unroll
   for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
   float den = 0.f;
-  for (int s = 0; s < kvs; ++s) {
-    const float2 ml = part_ml[s * total + w];
-    const float wgt = ml.y * exp2f(ml.x - mmax);
+  for (int i = 0; i < np; ++i) {
+    const float2 ml = ml_of(i);
+    // a group without keys has (max, sum) = (-inf, 0): weight 0
+    const float wgt = ml.y > 0.f ? ml.y * exp2f(ml.x - mmax) : 0.f;
     den += wgt;
-    const float* src = part_o + (s * total + w) * D + lane * kPer;
+    const int g = i / kvs, s = i - g * kvs;
+    const float* src = reinterpret_cast<const float*>(reinterpret_cast<const char*>(part_o) +
+                                                      g * group_bytes) +
+                       (s * total + w) * D + lane * kPer;
     if constexpr (kPer == 4) {
       const float4 v = *reinterpret_cast<const float4*>(src);
       acc[0] += wgt * v.x;
@@ -740,7 +759,7 @@ static int launch(Params& prm, int B, int Lq, int H, cudaStream_t stream) {
   dim3 grid(H, prm.mode == 0 ? nq / 2 + (nq & 1) : nq * prm.kv_splits, B);
   attn_fwd_kernel<D><<<grid, kThreads, C::kSmemAlloc, stream>>>(prm);
   int st = check_cuda(cudaGetLastError(), "attention: launch");
-  if (st || prm.kv_splits <= 1) return st;
+  if (st || prm.kv_splits <= 1 || prm.partial_only) return st;
   const int64_t warps = static_cast<int64_t>(B) * Lq * H;
   OutPlace op;
   op.out = prm.out;
@@ -753,7 +772,7 @@ static int launch(Params& prm, int B, int Lq, int H, cudaStream_t stream) {
   op.gate_bs = prm.gate_bs;
   op.gate_rs = prm.gate_rs;
   combine_kernel<D><<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(
-      prm.part_o, prm.part_ml, prm.kv_splits, B, Lq, H, op);
+      prm.part_o, prm.part_ml, prm.kv_splits, 1, 0, B, Lq, H, op);
   return check_cuda(cudaGetLastError(), "attention: combine launch");
 }
 
@@ -764,10 +783,20 @@ struct Plan {
   int kv_splits;
 };
 
-static int64_t split_ws_bytes(int kvs, int B, int Lq, int H, int D) {
-  if (kvs <= 1) return 0;
+// Partial outputs of kvs key ranges: [kvs][B][Lq][H][D] fp32, then (at the
+// next multiple of 256 bytes from the start, so that the layout does not
+// depend on the buffer's address) [kvs][B][Lq][H] (max, sum).
+static int64_t partial_ml_offset(int64_t rows, int D) {
+  return (rows * D * 4 + 255) / 256 * 256;
+}
+
+static int64_t partial_bytes(int kvs, int B, int Lq, int H, int D) {
   const int64_t rows = static_cast<int64_t>(kvs) * B * Lq * H;
   return rows * D * 4 + rows * 8 + 256;
+}
+
+static int64_t split_ws_bytes(int kvs, int B, int Lq, int H, int D) {
+  return kvs <= 1 ? 0 : partial_bytes(kvs, B, Lq, H, D);
 }
 
 static int sm_count() {
@@ -814,6 +843,24 @@ static Plan make_plan(int B, int Lq, int H, int D, int n_tiles, int64_t ws_bytes
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
       best = Plan{1, s};
+    }
+  }
+  return best;
+}
+
+// Key ranges per query tile for an export (every CTA a split CTA).
+static int best_splits(int B, int Lq, int H, int n_tiles) {
+  const int sms = sm_count();
+  const int64_t ctas1 = static_cast<int64_t>(H) * B * ((Lq + BM - 1) / BM);
+  const double c0 = kFixedLaneSteps / std::max(1.0, 0.5 * n_tiles);
+  const int s_max = std::max(1, std::min(32, n_tiles / 2));
+  int best = 1;
+  double best_cost = 1e300;
+  for (int s = 1; s <= s_max; ++s) {
+    const double cost = static_cast<double>((ctas1 * s + sms - 1) / sms) * (1.0 / s + c0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = s;
     }
   }
   return best;
@@ -878,6 +925,19 @@ static int attention_impl(const void* q, int64_t q_batch_stride, int64_t q_row_s
   if (D != 64 && D != 128) return set_error(TM_ERR_UNSUPPORTED, "attention: head dim %d", D);
   if (B < 1 || Lq < 1 || H < 1 || B > 65535 || H > 65535 || (Lq + 255) / 256 > 65535)
     return set_error(TM_ERR_INVALID_ARGUMENT, "attention: B=%d Lq=%d H=%d", B, Lq, H);
+  const bool export_parts = ext.parts != nullptr;
+  if (export_parts) {
+    // partial results only: `out` and everything about its placement go unused
+    if (ext.part_splits < 1 || ext.parts_bytes < partial_bytes(ext.part_splits, B, Lq, H, D))
+      return set_error(TM_ERR_INVALID_ARGUMENT, "attention: %d key ranges need %lld bytes of parts",
+                       ext.part_splits,
+                       (long long)partial_bytes(std::max(1, ext.part_splits), B, Lq, H, D));
+    if (!aligned16(ext.parts))
+      return set_error(TM_ERR_ALIGNMENT, "attention: parts not 16-byte aligned");
+    out = ext.parts;
+    out_batch_stride = 0;
+    out_row_stride = static_cast<int64_t>(H) * D;
+  }
   if (!q || !out || !spans || n_spans < 1)
     return set_error(TM_ERR_INVALID_ARGUMENT, "attention: null pointer or no spans");
   if (!aligned16(q) || !aligned16(out))
@@ -937,6 +997,25 @@ static int attention_impl(const void* q, int64_t q_batch_stride, int64_t q_row_s
   prm.out = static_cast<__nv_bfloat16*>(out);
   prm.out_bs = (B == 1) ? 0 : out_batch_stride;
   prm.out_rs = out_row_stride;
+  if (export_parts) {
+    if (ext.part_splits > nt)
+      return set_error(TM_ERR_INVALID_ARGUMENT, "attention: %d key ranges over %d key tiles",
+                       ext.part_splits, nt);
+    prm.rows_per_rank = Lq;
+    prm.mode = 1;
+    prm.kv_splits = ext.part_splits;
+    prm.partial_only = 1;
+    const int64_t rows = static_cast<int64_t>(ext.part_splits) * B * Lq * H;
+    prm.part_o = static_cast<float*>(ext.parts);
+    prm.part_ml = reinterpret_cast<float2*>(reinterpret_cast<char*>(prm.part_o) +
+                                            partial_ml_offset(rows, D));
+    const double sc = (scale > 0.f) ? (double)scale : 1.0 / std::sqrt((double)D);
+    prm.scale_log2 = static_cast<float>(sc * 1.4426950408889634);
+    prm.err = device_error_flag();
+    if (!prm.err) return set_error(TM_ERR_CUDA, "attention: device error flag unavailable");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return D == 128 ? launch<128>(prm, B, Lq, H, s) : launch<64>(prm, B, Lq, H, s);
+  }
   prm.rows_per_rank = ext.rows_per_rank > 0 ? ext.rows_per_rank : Lq;
   prm.head_base = ext.head_base;
   if (ext.rows_per_rank < 0 || ext.head_base < 0 ||
@@ -973,9 +1052,8 @@ static int attention_impl(const void* q, int64_t q_batch_stride, int64_t q_row_s
   if (plan.kv_splits > 1) {
     const int64_t rows = static_cast<int64_t>(plan.kv_splits) * B * Lq * H;
     prm.part_o = static_cast<float*>(workspace);
-    uintptr_t ml = reinterpret_cast<uintptr_t>(prm.part_o + rows * D);
-    ml = (ml + 255) & ~static_cast<uintptr_t>(255);
-    prm.part_ml = reinterpret_cast<float2*>(ml);
+    prm.part_ml = reinterpret_cast<float2*>(reinterpret_cast<char*>(prm.part_o) +
+                                            partial_ml_offset(rows, D));
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return D == 128 ? launch<128>(prm, B, Lq, H, s) : launch<64>(prm, B, Lq, H, s);
@@ -1018,6 +1096,66 @@ extern "C" int64_t tm_attention_workspace_bytes(int B, int Lq, int H, int D,
   const int64_t tiles = std::min<int64_t>((visible_keys + BN - 1) / BN, kMaxTiles);
   const Plan plan = make_plan(B, Lq, H, D, static_cast<int>(tiles), INT64_MAX);
   return split_ws_bytes(plan.kv_splits, B, Lq, H, D);
+}
+
+extern "C" int64_t tm_attention_partial_bytes(int B, int Lq, int H, int D, int splits) {
+  using namespace tmb::attn;
+  if (B < 1 || Lq < 1 || H < 1 || (D != 64 && D != 128) || splits < 1) return 0;
+  return partial_bytes(splits, B, Lq, H, D);
+}
+
+extern "C" int tm_attention_partial_splits(int B, int Lq, int H, int D, int64_t visible_keys) {
+  using namespace tmb::attn;
+  if (B < 1 || Lq < 1 || H < 1 || (D != 64 && D != 128) || visible_keys < 1) return 1;
+  const int tiles = static_cast<int>(std::min<int64_t>((visible_keys + BN - 1) / BN, kMaxTiles));
+  return best_splits(B, Lq, H, tiles);
+}
+
+extern "C" int tm_attention_combine(const void* parts, int n_groups, int64_t group_bytes,
+                                    int splits, int B, int Lq, int H, int D, void* out,
+                                    int64_t out_batch_stride, int64_t out_row_stride,
+                                    const void* gate_logits, int64_t gate_batch_stride,
+                                    int64_t gate_row_stride, void* stream) {
+  using namespace tmb::attn;
+  if (D != 64 && D != 128) return set_error(TM_ERR_UNSUPPORTED, "combine: head dim %d", D);
+  if (B < 1 || Lq < 1 || H < 1 || n_groups < 1 || splits < 1 || !parts || !out)
+    return set_error(TM_ERR_INVALID_ARGUMENT, "combine: B=%d Lq=%d H=%d groups=%d splits=%d",
+                     B, Lq, H, n_groups, splits);
+  const int64_t need = partial_bytes(splits, B, Lq, H, D);
+  if (n_groups > 1 && group_bytes < need)
+    return set_error(TM_ERR_INVALID_ARGUMENT, "combine: group stride %lld below %lld bytes",
+                     (long long)group_bytes, (long long)need);
+  if (!aligned16(parts) || (group_bytes & 15))
+    return set_error(TM_ERR_ALIGNMENT, "combine: parts or group stride not 16-byte aligned");
+  if (!aligned16(out) || (out_row_stride & 7) || (out_batch_stride & 7) ||
+      out_row_stride < static_cast<int64_t>(H) * D)
+    return set_error(TM_ERR_ALIGNMENT, "combine: output alignment or strides");
+  if (gate_logits && (gate_row_stride < H || gate_batch_stride < 0))
+    return set_error(TM_ERR_INVALID_ARGUMENT, "combine: gate row stride %lld < H",
+                     (long long)gate_row_stride);
+  const int64_t rows = static_cast<int64_t>(splits) * B * Lq * H;
+  const float* po = static_cast<const float*>(parts);
+  const float2* ml = reinterpret_cast<const float2*>(reinterpret_cast<const char*>(po) +
+                                                     partial_ml_offset(rows, D));
+  OutPlace op;
+  memset(&op, 0, sizeof(op));
+  op.out = static_cast<__nv_bfloat16*>(out);
+  op.out_bs = (B == 1) ? 0 : out_batch_stride;
+  op.out_rs = out_row_stride;
+  op.rows_per_rank = Lq;
+  op.gate = static_cast<const __nv_bfloat16*>(gate_logits);
+  op.gate_bs = (B == 1) ? 0 : gate_batch_stride;
+  op.gate_rs = gate_row_stride;
+  const int64_t warps = static_cast<int64_t>(B) * Lq * H;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>((warps + 7) / 8);
+  if (D == 128)
+    combine_kernel<128><<<grid, 256, 0, s>>>(po, ml, splits,
+                                             n_groups, group_bytes, B, Lq, H, op);
+  else
+    combine_kernel<64><<<grid, 256, 0, s>>>(po, ml, splits,
+                                            n_groups, group_bytes, B, Lq, H, op);
+  return check_cuda(cudaGetLastError(), "combine: launch");
 }
 
 extern "C" int tm_attention_tiles(const tm_kv_span* spans, int n_spans, int64_t cache_rows,

@@ -168,14 +168,17 @@ def rope_tables(cfg: StreamConfig, frames: int, audio_tokens: int, video_start: 
 def arena_cache(cfg: StreamConfig, video_rows: int, audio_rows: int, sp: int = 1,
                 slots: int = 6, device=None) -> KVCache:
     """Empty per-layer slot arenas for the four cache pairs: video self-attention
-    head-sharded over the ``sp`` ranks (reference layout), audio self-attention,
-    A2V (audio keys) and V2A (video keys) with all heads (the audio stream is
-    replicated)."""
+    head-sharded over the ``sp`` ranks (reference layout), audio self-attention
+    and A2V (audio keys) with all heads (the audio stream is replicated), V2A
+    (video keys) with all heads for this rank's 1 / ``sp`` of the video
+    tokens (the split-key V2A)."""
+    if video_rows % sp:
+        raise ValueError(f"{video_rows} video rows do not split over {sp} ranks")
     specs = {
         "video_self": ArenaSpec(slots, video_rows, cfg.video_heads // sp, cfg.video_dim_head),
         "audio_self": ArenaSpec(slots, audio_rows, cfg.audio_heads, cfg.audio_dim_head),
         "a2v": ArenaSpec(slots, audio_rows, cfg.audio_heads, cfg.audio_dim_head),
-        "v2a": ArenaSpec(slots, video_rows, cfg.audio_heads, cfg.audio_dim_head),
+        "v2a": ArenaSpec(slots, video_rows // sp, cfg.audio_heads, cfg.audio_dim_head),
     }
     return init_arena_cache(cfg.layers, specs, device=device)
 

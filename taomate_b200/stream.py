@@ -8,20 +8,26 @@ record, then the streaming eviction (``retain_streaming_context``: sink
 segment + two newest, taomate/inference/cache.py:58-67), from
 ``evict_from_block`` on.
 
-Execution: eager until the cache reaches its steady-state layout (sink + 2
-window blocks), then one forward is captured as a CUDA graph
-(:class:`taomate_b200.graphs.AttentionGraph`) and replayed for all four
-forwards of every later block; per block only the attention key-tile table
-(the new arena layout), the RoPE tables, the conditioning rows and the
-latents change, and each is written into the graph's own buffers by a kernel
-copy.  The text K/V of every layer are projected once per block by a second
-captured graph (the reference projects them in every forward unless its text
-K/V cache is on, which keeps them per prompt).
+Execution: the first block runs eagerly (it initialises cuBLAS, NCCL and the
+text K/V cache).  Every later forward runs from a CUDA graph
+(:class:`taomate_b200.graphs.AttentionGraph`) chosen by the forward's layout:
+its chunk geometry and the row count of every cache span it attends.  A
+layout seen for the first time is captured once, then replayed wherever it
+recurs: the four forwards of a block, every steady-state block (sink + 2
+window blocks), and the sigma = 0 re-prefill forwards of each conditioning
+refresh, whose layouts are those of the first window's blocks 0-2.  Per
+replay only the attention key-tile table (the new arena layout), the RoPE
+tables, the conditioning rows and the latents change, and each is written
+into the graph's own buffers by a kernel copy.  The text K/V of every layer
+are projected once per block by a separate captured graph (the reference
+projects them in every forward unless its text K/V cache is on, which keeps
+them per prompt).
 """
 
 from __future__ import annotations
 
 import time
+from collections import OrderedDict
 from dataclasses import dataclass, fields
 from typing import List, Optional, Sequence, Tuple
 
@@ -55,16 +61,40 @@ def block_geometry(k: int, cfg: StreamConfig, first_frames: int = 4, frames: int
     return frames, audio, first_frames + frames * (k - 1), audio_first + audio * (k - 1)
 
 
-def _flat_nbytes(ts: Sequence[torch.Tensor]) -> int:
-    return sum((t.numel() * t.element_size() + 15) // 16 * 16 for t in ts)
+class _Forward:
+    """One captured forward: its graph, the fixed buffers it reads (RoPE
+    tables, conditioning rows, latents) and writes (the denoised latents and
+    this forward's K/V chunk of every cache field)."""
+
+    def __init__(self, runner: "StreamRunner", k: int, v: torch.Tensor, a: torch.Tensor,
+                 cond: Conditioning, cache: KVCache):
+        pe, off = runner._pe(k)
+        self.pe = [t for pair in pe for t in pair]  # fresh tensors: the graph's own
+        self.cond = [getattr(cond, n).clone() for n in COND_FIELDS]
+        self.v, self.a = v.clone(), a.clone()
+        scond = Conditioning(**dict(zip(COND_FIELDS, self.cond)), video_ctx=runner.ctx[0],
+                             audio_ctx=runner.ctx[1], pe=pe)
+        self.graph = AttentionGraph(runner.dev, max_sites=6 * runner.cfg.layers)
+        with torch.no_grad():
+            self.out_v, self.out_a, new = self.graph.capture(
+                model_forward, runner.model, self.v, self.a, scond, cache,
+                video_token_offset=off)
+        # the chunk tensors only: views of ``new`` would keep capture-time slots referenced
+        self.chunks = [[last_chunk(getattr(lay, kf)) for kf, _ in FIELD_PAIRS]
+                       for lay in new.layers]
+
+    def release(self) -> None:
+        self.graph.reset()
 
 
 class StreamRunner:
     """Runs blocks of one stream on this rank.  ``sp``/``rank``: the sequence
-    parallel layout (video tokens split, audio replicated)."""
+    parallel layout (video tokens split, audio replicated).  ``max_graphs``:
+    captured forward layouts kept (least recently used dropped first)."""
 
     def __init__(self, model: CausalModelWeights, device, sp: int = 1, rank: int = 0,
-                 graphed: bool = True, evict_from_block: int = 0, slots: int = 6):
+                 graphed: bool = True, evict_from_block: int = 0, slots: int = 6,
+                 max_graphs: int = 6):
         self.model, self.cfg, self.dev = model, model.cfg, torch.device(device)
         self.sp, self.rank, self.graphed = sp, rank, graphed
         self.evict_from_block = evict_from_block
@@ -73,13 +103,23 @@ class StreamRunner:
         self.cache = arena_cache(cfg, ff * cfg.frame_tokens, fa, sp, slots, device=self.dev)
         attach_segments(self.cache, [])
         self.block = 0
-        self.graph: Optional[AttentionGraph] = None
+        self.graphs: "OrderedDict[tuple, _Forward]" = OrderedDict()
+        self.max_graphs = max_graphs
+        self.captures = 0
         self.text_graph: Optional[torch.cuda.CUDAGraph] = None
+        self._warm = False  # an eager forward ran since the text K/V cache was last cleared
         self.ctx = None  # (video_ctx, audio_ctx) of the current prompt
         self.latents = {}  # block_idx -> committed clean latents of the retained blocks
         self.refreshes = 0
         self.host_ms = {}  # host time of the replayed blocks, by phase
         self.host_blocks = 0
+
+    @property
+    def graph(self) -> Optional[AttentionGraph]:
+        """The most recently used captured forward (None: nothing captured)."""
+        if not self.graphs:
+            return None
+        return next(reversed(self.graphs.values())).graph
 
     # -- geometry -------------------------------------------------------------
     def local_tokens(self, frames: int) -> Tuple[int, int]:
@@ -88,13 +128,6 @@ class StreamRunner:
             raise ValueError(f"{L} video tokens do not split over {self.sp} ranks")
         n = L // self.sp
         return n, self.rank * n
-
-    def steady(self) -> bool:
-        """The cache holds the sink block and two window blocks and eviction is
-        on: this and every later block see the same number of key tiles per
-        attention."""
-        return (self.block >= max(3, self.evict_from_block)
-                and len(cache_segments(self.cache)) == 3)
 
     # -- one forward ------------------------------------------------------------
     def _cond(self, c: Conditioning, pe) -> Conditioning:
@@ -112,7 +145,7 @@ class StreamRunner:
             self.ctx[0].copy_(video_ctx)
             self.ctx[1].copy_(audio_ctx)
         if self.text_graph is not None:
-            self.text_graph.replay()  # re-project into the entries the forward graph reads
+            self.text_graph.replay()  # re-project into the entries the forward graphs read
         else:
             # the text K/V cache is keyed by the context tensor's identity, which
             # stays: drop its entries so the next forward projects the new prompt
@@ -120,6 +153,10 @@ class StreamRunner:
                 for attn in (blk.attn2, blk.audio_attn2):
                     if hasattr(attn, "_ltx_text_cross_kv_cache"):
                         attn._ltx_text_cross_kv_cache.clear()
+            self._warm = False  # the next forward projects them eagerly
+
+    def _use_graphs(self) -> bool:
+        return self.graphed and self._warm
 
     # -- the block ------------------------------------------------------------
     def run_block(self, video_latent: torch.Tensor, audio_latent: torch.Tensor,
@@ -127,9 +164,7 @@ class StreamRunner:
         """Denoise the block's latents (``[1, Lv_local, C]``, ``[1, La, C]``)
         with ``conds[0..2]``, commit with ``conds[3]``; returns the denoised
         latents (fresh tensors)."""
-        if self.graphed and self.graph is None and self.steady():
-            self._capture(video_latent, audio_latent, conds)
-        if self.graph is not None and self.steady():
+        if self._use_graphs():
             return self._replay_block(video_latent, audio_latent, conds)
         return self._eager_block(video_latent, audio_latent, conds)
 
@@ -148,7 +183,8 @@ class StreamRunner:
         the video self-attention K/V is taken from the rebuilt cache (no data
         moves).  The rebuilt rows go to free slots of the same arenas, so a
         captured forward keeps reading them.  ``conds[block_idx]``: the
-        block's sigma = 0 conditioning rows."""
+        block's sigma = 0 conditioning rows.  The forwards replay the graphs
+        of their layouts (those of the first window's blocks 0-2)."""
         segs = cache_segments(self.cache)
         if not segs:
             raise RuntimeError("The retained cache has no block metadata.")
@@ -163,12 +199,21 @@ class StreamRunner:
             for seg in segs:
                 k = int(seg["block_idx"])
                 v, a = self.latents[k]
-                pe, off = self._pe(k)
-                _, _, rebuilt = model_forward(self.model, v, a, self._cond(conds[k], pe), rebuilt,
-                                              kv_cache_only=True, video_token_offset=off)
-                for lay in rebuilt.layers:
-                    for kf, _ in FIELD_PAIRS:
-                        getattr(lay, kf).entries()
+                if self._use_graphs():
+                    g, spans = self._graph_for(k, v, a, conds[k], rebuilt)
+                    pe, _ = self._pe(k)
+                    self._load(g.pe, [t for pair in pe for t in pair])
+                    self._load([g.v, g.a] + g.cond,
+                               [v, a] + [getattr(conds[k], n) for n in COND_FIELDS])
+                    g.graph.replay(spans)
+                    rebuilt = self._appended(rebuilt, g.chunks)
+                else:
+                    pe, off = self._pe(k)
+                    _, _, rebuilt = model_forward(self.model, v, a, self._cond(conds[k], pe),
+                                                  rebuilt, kv_cache_only=True,
+                                                  video_token_offset=off)
+                    self._warm = True
+                flush_many([getattr(lay, kf) for lay in rebuilt.layers for kf, _ in FIELD_PAIRS])
         self.cache = replace_modal_fields(self.cache, rebuilt)
         self.refreshes += 1
 
@@ -209,52 +254,56 @@ class StreamRunner:
                 x_a = torch.add(x_a, ao, alpha=dt)
             _, _, new = model_forward(self.model, x_v, x_a, self._cond(conds[3], pe), self.cache,
                                       kv_cache_only=True, video_token_offset=off)
+        self._warm = True
         self._commit(new, (x_v, x_a))
         return x_v, x_a
 
     # -- graph executor -------------------------------------------------------
-    def _spans(self, cache: KVCache):
-        """Key spans of every cached attention of a forward, keyed by the
-        site's cache arena (the text cross-attention sites keep theirs)."""
-        F_, La, _, _ = block_geometry(self.block, self.cfg)
+    def _spans(self, cache: KVCache, k: int):
+        """Key spans of every cached attention of a forward of block ``k``
+        over ``cache``, keyed by the site's cache arena (the text
+        cross-attention sites keep theirs)."""
+        F_, La, _, _ = block_geometry(k, self.cfg)
         Lv = F_ * self.cfg.frame_tokens
+        Lv_local, _ = self.local_tokens(F_)  # V2A keys: this rank's video tokens
         out = {}
         for lay in cache.layers:
-            for (kf, vf), new_rows in zip(FIELD_PAIRS, (Lv, La, La, Lv)):
-                k, v = getattr(lay, kf), getattr(lay, vf)
-                out[k.arena.k.data_ptr()] = attention_spans(k, v, new_rows)
+            for (kf, vf), new_rows in zip(FIELD_PAIRS, (Lv, La, La, Lv_local)):
+                kv, vv = getattr(lay, kf), getattr(lay, vf)
+                out[kv.arena.k.data_ptr()] = attention_spans(kv, vv, new_rows)
         return out
 
-    def _capture(self, v, a, conds):
-        """Capture one steady-state forward (and the text K/V projection)."""
-        pe, off = self._pe(self.block)
-        self._static_pe = [t for pair in pe for t in pair]
-        cond0 = self._cond(conds[0], pe)
-        self._static_cond = [getattr(cond0, n).clone() for n in COND_FIELDS]
-        self._sv, self._sa = v.clone(), a.clone()
-        scond = Conditioning(**{n: t for n, t in zip(COND_FIELDS, self._static_cond)},
-                             video_ctx=self.ctx[0], audio_ctx=self.ctx[1], pe=pe)
-        for lay in self.cache.layers:  # pending chunks into their slots before capture
-            for kf, vf in FIELD_PAIRS:
-                getattr(lay, kf).entries()
-        # one eager forward first (cuBLAS / NCCL initialisation, text K/V cache warm)
-        with torch.no_grad():
-            model_forward(self.model, self._sv, self._sa, scond, self.cache,
-                          video_token_offset=off)
-        torch.cuda.synchronize(self.dev)
-        self.graph = AttentionGraph(self.dev, max_sites=6 * self.cfg.layers)
-        with torch.no_grad():
-            self._out_v, self._out_a, self._new = self.graph.capture(
-                model_forward, self.model, self._sv, self._sa, scond, self.cache,
-                video_token_offset=off)
-        self._chunks = [[last_chunk(getattr(lay, kf)) for kf, _ in FIELD_PAIRS]
-                        for lay in self._new.layers]
-        self._new = None  # its views would keep the capture-time slots referenced
-        self._capture_text()
+    @staticmethod
+    def _layout(spans: dict) -> tuple:
+        """What a captured forward fixes: the row count of every key span of
+        every site (the tile counts follow from it)."""
+        return tuple((key, tuple((src, rows) for src, _, rows in sp))
+                     for key, sp in sorted(spans.items()))
+
+    def _graph_for(self, k: int, v, a, cond: Conditioning, cache: KVCache):
+        """The captured forward of block ``k``'s geometry over ``cache``'s
+        layout (captured now if this layout is new) and the spans to replay
+        it with."""
+        spans = self._spans(cache, k)  # also copies pending chunks into their slots
+        F_, La, _, _ = block_geometry(k, self.cfg)
+        sig = (F_, La, self._layout(spans))
+        g = self.graphs.get(sig)
+        if g is not None:
+            self.graphs.move_to_end(sig)
+            return g, spans
+        while len(self.graphs) >= self.max_graphs:
+            _, old = self.graphs.popitem(last=False)
+            old.release()
+        g = _Forward(self, k, v, a, cond, cache)
+        self.graphs[sig] = g
+        self.captures += 1
+        if self.text_graph is None:
+            self._capture_text()
+        return g, spans
 
     def _capture_text(self):
         """A graph that re-projects the text K/V of every layer into the
-        buffers the forward graph reads (the text K/V cache entries)."""
+        buffers the forward graphs read (the text K/V cache entries)."""
         jobs = []
         for blk in self.model.transformer_blocks:
             for attn, ctx in ((blk.attn2, self.ctx[0]), (blk.audio_attn2, self.ctx[1])):
@@ -284,31 +333,36 @@ class StreamRunner:
             copy_bytes(d.data_ptr(), s.data_ptr(), (d.numel() * d.element_size() + 15) // 16 * 16,
                        self.dev)
 
-    def _replay_block(self, v, a, conds):
-        t0 = time.perf_counter()
-        pe, off = self._pe(self.block)
-        self._load(self._static_pe, [t for pair in pe for t in pair])
-        self._load([self._sv, self._sa], [v, a])
-        self.text_graph.replay()
-        spans = self._spans(self.cache)
-        t1 = time.perf_counter()
-        for fwd in range(4):
-            self._load(self._static_cond, [getattr(conds[fwd], n) for n in COND_FIELDS])
-            self.graph.replay(spans if fwd == 0 else None)
-            if fwd < 3:
-                dt = SIGMAS[fwd + 1] - SIGMAS[fwd]
-                self._sv.add_(self._out_v, alpha=dt)
-                self._sa.add_(self._out_a, alpha=dt)
-        t2 = time.perf_counter()
-        # commit: this block's K/V (the fourth replay's) appended to the cache
+    @staticmethod
+    def _appended(cache: KVCache, chunks) -> KVCache:
+        """``cache`` with a captured forward's K/V chunk appended to every field."""
         layers = []
-        for lay, chunks in zip(self.cache.layers, self._chunks):
+        for lay, lay_chunks in zip(cache.layers, chunks):
             kw = {}
-            for (kf, vf), (nk, nv) in zip(FIELD_PAIRS, chunks):
+            for (kf, vf), (nk, nv) in zip(FIELD_PAIRS, lay_chunks):
                 kw[kf], kw[vf] = cat_cache_pair(getattr(lay, kf), getattr(lay, vf), nk, nv)
             layers.append(LayerKVCache(**kw))
-        clean = (self._sv.clone(), self._sa.clone())
-        self._commit(KVCache(layers=layers), clean)
+        return KVCache(layers=layers)
+
+    def _replay_block(self, v, a, conds):
+        t0 = time.perf_counter()
+        g, spans = self._graph_for(self.block, v, a, conds[0], self.cache)
+        pe, _ = self._pe(self.block)
+        self._load(g.pe, [t for pair in pe for t in pair])
+        self._load([g.v, g.a], [v, a])
+        self.text_graph.replay()
+        t1 = time.perf_counter()
+        for fwd in range(4):
+            self._load(g.cond, [getattr(conds[fwd], n) for n in COND_FIELDS])
+            g.graph.replay(spans if fwd == 0 else None)
+            if fwd < 3:
+                dt = SIGMAS[fwd + 1] - SIGMAS[fwd]
+                g.v.add_(g.out_v, alpha=dt)
+                g.a.add_(g.out_a, alpha=dt)
+        t2 = time.perf_counter()
+        # commit: this block's K/V (the fourth replay's) appended to the cache
+        clean = (g.v.clone(), g.a.clone())
+        self._commit(self._appended(self.cache, g.chunks), clean)
         t3 = time.perf_counter()
         for k, dt in (("prepare", t1 - t0), ("replays", t2 - t1), ("commit_evict", t3 - t2)):
             self.host_ms[k] = self.host_ms.get(k, 0.0) + dt * 1e3
@@ -317,7 +371,7 @@ class StreamRunner:
 
     def release(self):
         """Drop the captured graphs (before the process group goes away)."""
-        if self.graph is not None:
-            self.graph.reset()
-        self.graph = None
+        for g in self.graphs.values():
+            g.release()
+        self.graphs.clear()
         self.text_graph = None

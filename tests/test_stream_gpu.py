@@ -5,9 +5,10 @@ frame, audio 4 heads x 64, text 24 tokens) runs the pipeline's schedule:
 block 0 of 4 frames, then blocks of 3 frames, each with 3 denoising forwards
 and a commit forward, eviction to the sink block + the 2 newest blocks.
 
-* The CUDA-graph executor (capture at the steady state, replay with a
-  rewritten key-tile table, kernel-copied inputs, per-block text K/V graph)
-  gives the same bits as issuing every forward eagerly.
+* The CUDA-graph executor (one capture per cache layout from block 1 on,
+  replayed with a rewritten key-tile table, kernel-copied inputs, per-block
+  text K/V graph) gives the same bits as issuing every forward eagerly; the
+  refresh forwards replay the first window's layouts.
 * The retained segments follow the reference policy ([0], [0,1], [0,1,2],
   [0,2,3], [0,3,4], ...) and the cache holds 3840-equivalent rows (sink + 2
   blocks) at the steady state.
@@ -60,14 +61,17 @@ def _run(graphed, n_blocks=7, prompt_change_at=5):
     torch.cuda.synchronize()
     rows = int(runner.cache.layers[0].video_self_k.shape[1])
     captured = runner.graph is not None
+    captures = runner.captures
     runner.release()
-    return outs, kept, rows, captured
+    return outs, kept, rows, captured, captures
 
 
 def test_graph_executor_equals_eager():
-    eo, ek, erows, ecap = _run(graphed=False)
-    go, gk, grows, gcap = _run(graphed=True)
+    eo, ek, erows, ecap, _ = _run(graphed=False)
+    go, gk, grows, gcap, gn = _run(graphed=True)
     assert not ecap and gcap
+    # block 0 eager; layouts [4], [4, 3], then the steady [4, 3, 3] for blocks 3-6
+    assert gn == 3
     assert ek == gk == [[0], [0, 1], [0, 1, 2], [0, 2, 3], [0, 3, 4], [0, 4, 5], [0, 5, 6]]
     assert erows == grows == (4 + 3 + 3) * 96
     for i, ((ev, ea), (gv, ga)) in enumerate(zip(eo, go)):
@@ -121,8 +125,9 @@ def _longform(graphed, segments=3, check=None):
         runner.end_segment()
     torch.cuda.synchronize()
     captured = runner.graph is not None
+    captures = runner.captures
     runner.release()
-    return outs, kept, captured
+    return outs, kept, captured, captures
 
 
 def _check_sink_rebuilt(runner, model, conds):
@@ -144,9 +149,12 @@ def _check_sink_rebuilt(runner, model, conds):
 
 
 def test_longform_refresh_graph_equals_eager():
-    eo, ek, ecap = _longform(graphed=False, check=_check_sink_rebuilt)
-    go, gk, gcap = _longform(graphed=True)
+    eo, ek, ecap, _ = _longform(graphed=False, check=_check_sink_rebuilt)
+    go, gk, gcap, gn = _longform(graphed=True, check=_check_sink_rebuilt)
     assert not ecap and gcap
+    # window 0: blocks 1-4 ([4], [4,3], [4,3,3], [4,3,3,3]); the first refresh adds the
+    # sink's empty-cache layout and replays blocks 1-2's; every later block is [4,3,3]
+    assert gn == 5
     # window 0 keeps every block; the window end and every later block evict
     assert ek == gk
     assert ek[4] == [0, 1, 2, 3, 4] and ek[5] == [0, 4, 5] and ek[14] == [0, 13, 14]
