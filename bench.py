@@ -69,6 +69,8 @@ def parse():
                          "the kernels' NVLink peer stores")
     ap.add_argument("--eager", action="store_true",
                     help="issue every forward from Python instead of replaying a CUDA graph")
+    ap.add_argument("--serial-audio", action="store_true",
+                    help="run each block's audio chain on the main stream (no second stream)")
     ap.add_argument("--qkv3", action="store_true",
                     help="three projection GEMMs per call instead of one over the fused weights")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -702,7 +704,8 @@ def c4_step(args, dev, rank, world, local, read_stream):
     prompt = synthetic_conditioning(cfg, 3, 25, dev, gen)
 
     def timed(n_steps, n_warm, host_io=False, sections=False):
-        runner = StreamRunner(model, dev, sp=world, rank=rank, graphed=not args.eager)
+        runner = StreamRunner(model, dev, sp=world, rank=rank, graphed=not args.eager,
+                              overlap_audio=not args.serial_audio)
         runner.set_prompt(prompt.video_ctx, prompt.audio_ctx)
         for k in range(n_warm):  # eager blocks until the steady state, then capture
             runner.run_block(*block_inputs(k))
@@ -711,6 +714,7 @@ def c4_step(args, dev, rank, world, local, read_stream):
         steady = [block_inputs(n_warm + i) for i in range(n_steps)]
         runner.run_block(*steady[0])  # capture (if not yet) + one replay, untimed
         TIMER.stop()
+        runner.host_ms, runner.host_blocks = {}, 0  # host time of the timed blocks only
         host = None
         if host_io:
             flat = lambda v, a, conds: [v, a] + [getattr(c, nm) for c in conds
@@ -872,7 +876,7 @@ def c5_longform(args, dev, rank, world, local):
         return v, a, [synthetic_conditioning(cfg, F_, La, dev, gen) for _ in range(4)]
 
     runner = StreamRunner(model, dev, sp=world, rank=rank, graphed=not args.eager,
-                          evict_from_block=per)
+                          evict_from_block=per, overlap_audio=not args.serial_audio)
     inputs = [block_inputs(k) for k in range(segs * per)]
     torch.cuda.synchronize()
     if world > 1:
@@ -1045,7 +1049,9 @@ def run_ours(args):
                                 device_id=dev)
         P.init_sp_mesh(world, world)
         if not args.nccl_exchange:
-            P.init_peer_exchange(1, Q_FRAMES * FRAME_TOKENS // world, HEADS, DIM_HEAD)
+            from taomate_b200.block import v2a_gather_bytes
+            P.init_peer_exchange(1, Q_FRAMES * FRAME_TOKENS // world, HEADS, DIM_HEAD,
+                                 gather_bytes=v2a_gather_bytes(26, 32, 64, world))
     read_stream = torch.cuda.Stream(dev)
     if args.workload == "c5":
         line = c5_longform(args, dev, rank, world, local)
@@ -1078,10 +1084,14 @@ def run_ours(args):
                 "parallelism": (f"ulysses sp{world} (video split by tokens, audio replicated), "
                                 "video self-attention exchanges "
                                 + ("nccl all_to_all" if args.nccl_exchange
-                                   else "fused NVLink peer stores") + ", V2A all-gather")
+                                   else "fused NVLink peer stores")
+                                + ", split-key V2A (partial results gathered over "
+                                + ("nccl)" if args.nccl_exchange else "NVLink)")
+                                + (", audio chain on the main stream" if args.serial_audio
+                                   else ", audio chain on a second stream"))
                                if world > 1 else "single gpu",
-                "executor": "eager" if args.eager else "cuda graph per forward (eager warm-up, "
-                                                       "capture at the steady state)",
+                "executor": "eager" if args.eager else "cuda graph per forward layout (block 0 "
+                                                       "eager, one capture per cache layout)",
                 "layers": args.layers,
                 "l2": "inputs larger than L2 (48 layers of weights ~38 GB, caches, activations), "
                       "no flush"},

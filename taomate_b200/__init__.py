@@ -16,7 +16,8 @@ The compute runs in ``lib/libtaomate_b200.so`` (C ABI: include/taomate_b200.h).
 from .rope import CausalRopeType, apply_split_rotary_emb, causal_precompute_freqs_cis
 from .attention import (_cross_modal_pair_attention_with_cache, attention_with_cache,
                         cross_modal_pair_attention_with_cache, flash_attention,
-                        fuse_qkv_weights, key_padding_runs, standard_attention_forward,
+                        fuse_kv_weights, fuse_qkv_weights, key_padding_runs,
+                        standard_attention_forward,
                         text_cross_attention_with_kv_cache)
 from .kv_cache import (ArenaKV, ArenaSpec, KVArena, KVCache, LayerKVCache, _cat_cache,
                        cat_cache_pair, init_arena_cache)
@@ -29,6 +30,7 @@ __all__ = [
     "CausalRopeType", "apply_split_rotary_emb", "causal_precompute_freqs_cis",
     "attention_with_cache", "flash_attention", "standard_attention_forward",
     "text_cross_attention_with_kv_cache", "key_padding_runs", "fuse_qkv_weights",
+    "fuse_kv_weights",
     "cross_modal_pair_attention_with_cache", "_cross_modal_pair_attention_with_cache",
     "ArenaKV", "ArenaSpec", "KVArena", "KVCache", "LayerKVCache", "_cat_cache",
     "cat_cache_pair", "init_arena_cache",

@@ -393,23 +393,12 @@ def _cache_source(cached_k, cached_v):
     return cached_k, cached_v, [(0, int(cached_k.shape[1]))]
 
 
-def fuse_qkv_weights(attn) -> bool:
-    """Lay ``to_q``, ``to_k`` and ``to_v`` of a self-attention module out as one
-    ``[3 * inner, in]`` weight buffer (and one bias buffer): the three
-    parameters become row blocks of it, with their values unchanged, so
-    ``attention_with_cache`` runs the three projections of a self-attention
-    call as ONE GEMM.  At the short chunks of a streaming step (1152 rows, or
-    1152 / G per GPU under sequence parallelism) one GEMM with three times the
-    columns fills the SMs better than three.  Returns False (and changes
-    nothing) when the three linears differ in shape, dtype, device or bias.
-
-    Reference counterpart: none (the reference runs the three linears,
-    ltx_causal/transformer/kv_cache.py:1380-1410); a loader calls this once
-    per module after loading weights.  Weights later loaded in place
-    (``load_state_dict``, ``copy_``) land in the shared buffer; a parameter
-    that is replaced by a new tensor ends the fusion for that module.
-    """
-    lins = (attn.to_q, attn.to_k, attn.to_v)
+def _fuse_linears(attn, names: Tuple[str, ...], tag: str) -> bool:
+    """Lay the linears ``names`` of ``attn`` out as one ``[n * out, in]``
+    weight buffer (and one bias buffer): the parameters become row blocks of
+    it, values unchanged.  False (nothing changed) when they differ in shape,
+    dtype, device or bias."""
+    lins = [getattr(attn, n) for n in names]
     ws = [l.weight for l in lins]
     bs = [l.bias for l in lins]
     w0 = ws[0]
@@ -427,24 +416,108 @@ def fuse_qkv_weights(attn) -> bool:
             l.weight.data = W[i * n:(i + 1) * n]
             if Bv is not None:
                 l.bias.data = Bv[i * n:(i + 1) * n]
-    attn._tm_qkv = (W, Bv)
+    setattr(attn, tag, (W, Bv))
     return True
 
 
-def _fused_qkv(attn):
-    """The fused QKV buffers of ``fuse_qkv_weights`` while the module's three
+def _fused(attn, names: Tuple[str, ...], tag: str):
+    """The fused buffers of :func:`_fuse_linears` while the module's
     parameters still point into them, else None."""
-    f = getattr(attn, "_tm_qkv", None)
+    f = getattr(attn, tag, None)
     if f is None:
         return None
     W, Bv = f
-    n = W.shape[0] // 3
-    for i, l in enumerate((attn.to_q, attn.to_k, attn.to_v)):
+    n = W.shape[0] // len(names)
+    for i, name in enumerate(names):
+        l = getattr(attn, name)
         if l.weight.data_ptr() != W[i * n].data_ptr() or l.weight.shape[0] != n:
             return None
         if Bv is not None and (l.bias is None or l.bias.data_ptr() != Bv[i * n:].data_ptr()):
             return None
     return f
+
+
+def fuse_qkv_weights(attn) -> bool:
+    """Lay ``to_q``, ``to_k`` and ``to_v`` of a self-attention module out as one
+    ``[3 * inner, in]`` weight buffer (and one bias buffer): the three
+    parameters become row blocks of it, with their values unchanged, so
+    ``attention_with_cache`` runs the three projections of a self-attention
+    call as ONE GEMM.  At the short chunks of a streaming step (1152 rows, or
+    1152 / G per GPU under sequence parallelism) one GEMM with three times the
+    columns fills the SMs better than three.  Returns False (and changes
+    nothing) when the three linears differ in shape, dtype, device or bias.
+
+    Reference counterpart: none (the reference runs the three linears,
+    ltx_causal/transformer/kv_cache.py:1380-1410); a loader calls this once
+    per module after loading weights.  Weights later loaded in place
+    (``load_state_dict``, ``copy_``) land in the shared buffer; a parameter
+    that is replaced by a new tensor ends the fusion for that module.
+    """
+    return _fuse_linears(attn, ("to_q", "to_k", "to_v"), "_tm_qkv")
+
+
+def fuse_kv_weights(attn) -> bool:
+    """``fuse_qkv_weights`` for the key and value projections of a
+    cross-attention module (``to_k``, ``to_v`` read the same context): one
+    ``[2 * inner, in]`` GEMM computes both (the A2V / V2A pair,
+    kv_cache.py:2011-2022)."""
+    return _fuse_linears(attn, ("to_k", "to_v"), "_tm_kv")
+
+
+def _fused_qkv(attn):
+    return _fused(attn, ("to_q", "to_k", "to_v"), "_tm_qkv")
+
+
+def _fused_kv(attn):
+    return _fused(attn, ("to_k", "to_v"), "_tm_kv")
+
+
+def kv_projection(attn, ctx: Tensor, pe, eps: float) -> Tuple[Tensor, Tensor]:
+    """Keys and values of a cross-attention call on one GPU: ``to_k`` /
+    ``to_v`` of ``ctx`` (one GEMM after :func:`fuse_kv_weights`), K
+    RMS-normalised and rotated by ``pe`` (None: no rotation) in one fused
+    launch; returns ``[B, L, H, D]`` views that share one row stride
+    (kv_cache.py:1380-1410 for the K/V side)."""
+    H, D = int(attn.heads), int(attn.dim_head)
+    B, L = int(ctx.shape[0]), int(ctx.shape[1])
+    f = _fused_kv(attn)
+    if f is not None:
+        k, v = F.linear(ctx, f[0], f[1]).split(f[0].shape[0] // 2, dim=-1)
+        (k,) = norm_rope([k], [attn.k_norm.weight], [pe], H, D, eps, inplace=True)
+        return k, v.unflatten(-1, (H, D))
+    k = F.linear(ctx, attn.to_k.weight, attn.to_k.bias)
+    v = F.linear(ctx, attn.to_v.weight, attn.to_v.bias)
+    (k,) = norm_rope([k], [attn.k_norm.weight], [pe], H, D, eps)
+    return k, v.view(B, L, H, D)
+
+
+def cross_attention_local(attn, x: Tensor, pe, k: Tensor, v: Tensor, cached_k, cached_v,
+                          new_kv_real_len: Optional[int] = None,
+                          profile_name: str = "cross") -> Tuple[Tensor, Tensor, Tensor]:
+    """``attention_with_cache`` on one GPU (or under ``sp_local``) for a
+    cross-attention whose keys and values were projected beforehand
+    (:func:`kv_projection`, e.g. on another stream): the query projection,
+    its norm + RoPE, attention over the cache spans and the new rows (the
+    per-head gate fused), ``to_out``.  Returns ``(out, new_k, new_v)`` as
+    ``attention_with_cache`` does (kv_cache.py:1148-1547)."""
+    H, D = int(attn.heads), int(attn.dim_head)
+    B = int(x.shape[0])
+    eps = _norm_eps(attn.q_norm)
+    with section(profile_name + ".qkv_proj_norm"):
+        q = F.linear(x, attn.to_q.weight, attn.to_q.bias)
+    with section(profile_name + ".rope_reshape"):
+        (q,) = norm_rope([q], [attn.q_norm.weight], [pe], H, D, eps)
+    n = int(k.shape[1])
+    if new_kv_real_len is not None and new_kv_real_len < n:
+        n = int(new_kv_real_len)
+        k, v = k[:, :n], v[:, :n]
+    ck, cv, spans = _cache_source(cached_k, cached_v)
+    glog = attn.to_gate_logits(x) if getattr(attn, "to_gate_logits", None) is not None else None
+    with section(profile_name + ".sdpa"):
+        out = flash_attention(q, ck, cv, spans, k, v, n, gate_logits=glog)
+    with section(profile_name + ".out_proj"):
+        out = attn.to_out(out.reshape(B, -1, H * D))
+    return out, k, v
 
 
 def _projections(attn, x: Tensor, ctx: Tensor):

@@ -42,7 +42,8 @@ from torch import Tensor
 from . import _lib
 from . import parallel as P
 from .attention import (AttentionWeights, _cache_source, _norm_eps, attention_with_cache,
-                        flash_attention, text_cross_attention_with_kv_cache)
+                        cross_attention_local, flash_attention, kv_projection,
+                        text_cross_attention_with_kv_cache)
 from .kv_cache import LayerKVCache, _cat_cache
 from .profiler import section
 from .rope import norm_rope
@@ -166,9 +167,22 @@ def feed_forward(ff, x: Tensor) -> Tensor:
     return F.linear(h, out.weight, out.bias)
 
 
+_V2A_MAX_PARTS = 8
+
+
+def v2a_gather_bytes(audio_tokens: int, heads: int, dim_head: int, sp: int) -> int:
+    """Bytes of one gather buffer of the split-key V2A for up to
+    ``audio_tokens`` audio queries on ``sp`` ranks (for
+    ``parallel.init_peer_exchange(gather_bytes=)``)."""
+    from .attention import partial_bytes
+    splits = max(1, _V2A_MAX_PARTS // sp)
+    return sp * partial_bytes(1, audio_tokens, heads, dim_head, splits)
+
+
 def video_to_audio_split_keys(attn, ax_v2a: Tensor, vx_v2a: Tensor, audio_cross_pe,
                               video_cross_pe, cached_k, cached_v,
-                              video_real_len: Optional[int] = None):
+                              video_real_len: Optional[int] = None,
+                              layer_idx: Optional[int] = None, kv=None):
     """V2A attention (audio queries over video keys) when the audio stream is
     replicated on every rank and the video stream is split by sequence.
 
@@ -182,23 +196,29 @@ def video_to_audio_split_keys(attn, ax_v2a: Tensor, vx_v2a: Tensor, audio_cross_
     parts, ~0.2 MB); one all-gather of those parts, and every rank merges all
     ranks' parts in the same order (tm_attention_combine, the per-head gate
     fused), so the output is the same softmax over all keys and the same bits
-    on every rank.  The V2A cache of each rank holds its own video tokens
-    (all heads); this call returns those new K/V."""
+    on every rank.  The all-gather is a copy into every peer's buffer over
+    NVLink plus a bounded flag handshake when the peer exchange holds gather
+    buffers (the buffer alternates with ``layer_idx``), NCCL otherwise.  The
+    V2A cache of each rank holds its own video tokens (all heads); this call
+    returns those new K/V.  ``kv``: this rank's K/V already projected
+    (:func:`taomate_b200.attention.kv_projection`); ``vx_v2a`` is then unused."""
     import torch.distributed as dist
     from .attention import combine_partials, partial_bytes, partial_splits
     G, grp, r = P.get_sp_world_size(), P.get_sp_group(), P.get_sp_rank()
     H, D = int(attn.heads), int(attn.dim_head)
-    B, Lloc, La = int(vx_v2a.shape[0]), int(vx_v2a.shape[1]), int(ax_v2a.shape[1])
+    src = kv[0] if kv is not None else vx_v2a
+    B, Lloc, La = int(src.shape[0]), int(src.shape[1]), int(ax_v2a.shape[1])
     if B != 1:
         raise NotImplementedError("the split-key V2A path takes batch 1")
     eps = _norm_eps(attn.q_norm)
     with section("video_to_audio.qkv_proj_norm"):
         q = F.linear(ax_v2a, attn.to_q.weight, attn.to_q.bias)
-        k = F.linear(vx_v2a, attn.to_k.weight, attn.to_k.bias)
-        v = F.linear(vx_v2a, attn.to_v.weight, attn.to_v.bias).view(B, Lloc, H, D)
+        if kv is None:
+            k, v = kv_projection(attn, vx_v2a, video_cross_pe, eps)
+        else:
+            k, v = kv
     with section("video_to_audio.rope_reshape"):
         (q,) = norm_rope([q], [attn.q_norm.weight], [audio_cross_pe], H, D, eps)
-        (k,) = norm_rope([k], [attn.k_norm.weight], [video_cross_pe], H, D, eps)
     n = Lloc  # this rank's real video rows of the chunk
     if video_real_len is not None:
         n = max(0, min(Lloc, int(video_real_len) - r * Lloc))
@@ -206,9 +226,15 @@ def video_to_audio_split_keys(attn, ax_v2a: Tensor, vx_v2a: Tensor, audio_cross_
     ck, cv, spans = _cache_source(cached_k, cached_v)
     cached = sum(int(rows) for _, rows in spans)
     # the same number of key ranges on every rank (ranks hold equal cache rows)
-    splits = partial_splits(B, La, H, D, cached + Lloc)
+    # at most 8 parts in all: past that, moving the parts costs more than the
+    # key-range split saves
+    splits = min(partial_splits(B, La, H, D, cached + Lloc), max(1, _V2A_MAX_PARTS // G))
     pb = partial_bytes(B, La, H, D, splits)
-    gathered = torch.empty(G * pb, dtype=torch.uint8, device=q.device)
+    peer = P.get_peer_exchange()
+    gathered = peer.gather_buffer(layer_idx or 0, pb) if peer is not None else None
+    if gathered is None:
+        peer = None
+        gathered = torch.empty(G * pb, dtype=torch.uint8, device=q.device)
     own = gathered[r * pb:(r + 1) * pb]
     with section("video_to_audio.sdpa"):
         if cached + n == 0:
@@ -221,7 +247,10 @@ def video_to_audio_split_keys(attn, ax_v2a: Tensor, vx_v2a: Tensor, audio_cross_
         else:
             flash_attention(q, ck, cv, spans, k, v, n, parts=own, part_splits=splits)
     with section("video_to_audio.all_gather"):
-        dist.all_gather_into_tensor(gathered, own, group=grp)
+        if peer is not None:
+            peer.all_gather_parts(gathered, pb)  # NVLink copies + a bounded handshake
+        else:
+            dist.all_gather_into_tensor(gathered, own, group=grp)
     with section("video_to_audio.combine"):
         glog = None
         if getattr(attn, "to_gate_logits", None) is not None:
@@ -400,7 +429,6 @@ def block_forward_with_cache(
         block.attn2, tin, v_ctx, mask=video_context_mask, base_context=video_ctx,
         prompt_cache_key=video_prompt_cache_key, cache_name="video_text_cross",
         layer_idx=layer_idx)
-    main.wait_stream(side)
 
     # the text cross residuals (gate 6:9 under cross_attention_adaln, none
     # otherwise), fused with the norms that follow
@@ -409,7 +437,11 @@ def block_forward_with_cache(
     new_a2v_k = new_a2v_v = new_v2a_k = new_v2a_v = None
     ffin_v = torch.empty_like(video_x)
     ffin_a = torch.empty_like(audio_x)
-    if not getattr(block, "skip_cross_modal_attention", False):
+    cross = not getattr(block, "skip_cross_modal_attention", False)
+    # one GPU, or replicated audio under sequence parallelism: the pair runs
+    # without exchanges inside it except V2A's gather of partial results
+    split_chains = audio_local or not P.is_sp_enabled()
+    if cross:
         # ── A2V / V2A (kv_cache.py:2512-2598): norm3 of both streams and the
         # four modulated inputs, from get_av_ca_ada_values (causal_block.py:454-478):
         # table[:4] + cross_ss -> (scale_a2v, shift_a2v, scale_v2a, shift_v2a),
@@ -418,50 +450,85 @@ def block_forward_with_cache(
                    video_frame_seqlen, video_token_offset)
         aca = _ada(block.scale_shift_table_a2v_ca_audio[:4], audio_cross_ss, La, 4, Da,
                    audio_frame_seqlen, audio_token_offset)
+        vg = _ada(block.scale_shift_table_a2v_ca_video[4:], video_cross_gate, Lv, 1, Dv,
+                  video_frame_seqlen, video_token_offset)
+        ag = _ada(block.scale_shift_table_a2v_ca_audio[4:], audio_cross_gate, La, 1, Da,
+                  audio_frame_seqlen, audio_token_offset)
         vx_a2v, vx_v2a = torch.empty_like(video_x), torch.empty_like(video_x)
         ax_a2v, ax_v2a = torch.empty_like(audio_x), torch.empty_like(audio_x)
+    if cross and split_chains:
+        # Each chain normalises its own stream and projects the keys and values
+        # that the other chain's attention reads (V2A's from the video tokens on
+        # the video chain, A2V's from the audio tokens on the audio chain); a
+        # chain waits for the other only where that attention starts.
+        a2v, v2a = block.audio_to_video_attn, block.video_to_audio_attn
+        with section("block.video_norm"):
+            residual_norm(vx, v_text, tgate_v, _TEXT_Q[2], vx,
+                          [(vx_a2v, vca, 0, 1), (vx_v2a, vca, 2, 3)], eps=eps)
+        with section("video_to_audio.kv_proj_norm"):
+            v2a_kv = kv_projection(v2a, vx_v2a, video_cross_pe, _norm_eps(v2a.q_norm))
+        v2a_ready = torch.cuda.Event()
+        v2a_ready.record(main)
+        with torch.cuda.stream(side):
+            with section("block.audio_norm"):
+                residual_norm(ax, a_text, tgate_a, _TEXT_Q[2], ax,
+                              [(ax_a2v, aca, 0, 1), (ax_v2a, aca, 2, 3)], eps=eps)
+            with section("audio_to_video.kv_proj_norm"):
+                a2v_kv = kv_projection(a2v, ax_a2v, audio_cross_pe, _norm_eps(a2v.q_norm))
+            a2v_ready = torch.cuda.Event()
+            a2v_ready.record(side)
+            # audio chain: V2A, gated residual + FFN input (slice 3:6)
+            side.wait_event(v2a_ready)
+            if audio_local:
+                v2a_out, new_v2a_k, new_v2a_v = video_to_audio_split_keys(
+                    v2a, ax_v2a, vx_v2a, audio_cross_pe, video_cross_pe, layer_cache.v2a_k,
+                    layer_cache.v2a_v, video_real_len, layer_idx, kv=v2a_kv)
+            else:
+                v2a_out, new_v2a_k, new_v2a_v = cross_attention_local(
+                    v2a, ax_v2a, audio_cross_pe, *v2a_kv, layer_cache.v2a_k, layer_cache.v2a_v,
+                    video_real_len, "video_to_audio")
+            with section("block.audio_norm"):
+                residual_norm(ax, v2a_out, ag, 0, ax, [(ffin_a, asrc, _MLP[1], _MLP[0])],
+                              eps=eps)
+        # video chain: A2V (this rank's video queries over all audio keys), gated
+        # residual + FFN input
+        main.wait_event(a2v_ready)
+        a2v_out, new_a2v_k, new_a2v_v = cross_attention_local(
+            a2v, vx_a2v, video_cross_pe, *a2v_kv, layer_cache.a2v_k, layer_cache.a2v_v,
+            audio_real_len, "audio_to_video")
+        with section("block.video_norm"):
+            residual_norm(vx, a2v_out, vg, 0, vx, [(ffin_v, vsrc, _MLP[1], _MLP[0])], eps=eps)
+    elif cross:
+        # the reference's layout under sequence parallelism (audio split too):
+        # both attentions exchange through the group, one after the other
+        main.wait_stream(side)
         with section("block.video_norm"):
             residual_norm(vx, v_text, tgate_v, _TEXT_Q[2], vx,
                           [(vx_a2v, vca, 0, 1), (vx_v2a, vca, 2, 3)], eps=eps)
         with section("block.audio_norm"):
             residual_norm(ax, a_text, tgate_a, _TEXT_Q[2], ax,
                           [(ax_a2v, aca, 0, 1), (ax_v2a, aca, 2, 3)], eps=eps)
-        vg = _ada(block.scale_shift_table_a2v_ca_video[4:], video_cross_gate, Lv, 1, Dv,
-                  video_frame_seqlen, video_token_offset)
-        ag = _ada(block.scale_shift_table_a2v_ca_audio[4:], audio_cross_gate, La, 1, Da,
-                  audio_frame_seqlen, audio_token_offset)
-        side.wait_stream(main)
-        # audio chain: V2A, gated residual + FFN input (slice 3:6), FFN
-        with torch.cuda.stream(side):
-            if audio_local:
-                v2a_out, new_v2a_k, new_v2a_v = video_to_audio_split_keys(
-                    block.video_to_audio_attn, ax_v2a, vx_v2a, audio_cross_pe, video_cross_pe,
-                    layer_cache.v2a_k, layer_cache.v2a_v, video_real_len)
-            else:
-                v2a_out, new_v2a_k, new_v2a_v = attention_with_cache(
-                    block.video_to_audio_attn, ax_v2a, vx_v2a, audio_cross_pe, video_cross_pe,
-                    layer_cache.v2a_k, layer_cache.v2a_v, new_kv_real_len=video_real_len,
-                    profile_name="video_to_audio")
-            with section("block.audio_norm"):
-                residual_norm(ax, v2a_out, ag, 0, ax, [(ffin_a, asrc, _MLP[1], _MLP[0])],
-                              eps=eps)
-        # video chain: A2V (replicated audio: this rank's video queries over all
-        # audio keys), gated residual + FFN input
-        with local():
-            a2v_out, new_a2v_k, new_a2v_v = attention_with_cache(
-                block.audio_to_video_attn, vx_a2v, ax_a2v, video_cross_pe, audio_cross_pe,
-                layer_cache.a2v_k, layer_cache.a2v_v, new_kv_real_len=audio_real_len,
-                profile_name="audio_to_video")
+        v2a_out, new_v2a_k, new_v2a_v = attention_with_cache(
+            block.video_to_audio_attn, ax_v2a, vx_v2a, audio_cross_pe, video_cross_pe,
+            layer_cache.v2a_k, layer_cache.v2a_v, new_kv_real_len=video_real_len,
+            profile_name="video_to_audio")
+        with section("block.audio_norm"):
+            residual_norm(ax, v2a_out, ag, 0, ax, [(ffin_a, asrc, _MLP[1], _MLP[0])], eps=eps)
+        a2v_out, new_a2v_k, new_a2v_v = attention_with_cache(
+            block.audio_to_video_attn, vx_a2v, ax_a2v, video_cross_pe, audio_cross_pe,
+            layer_cache.a2v_k, layer_cache.a2v_v, new_kv_real_len=audio_real_len,
+            profile_name="audio_to_video")
         with section("block.video_norm"):
             residual_norm(vx, a2v_out, vg, 0, vx, [(ffin_v, vsrc, _MLP[1], _MLP[0])], eps=eps)
+        side.wait_stream(main)
     else:
         with section("block.video_norm"):
             residual_norm(vx, v_text, tgate_v, _TEXT_Q[2], vx,
                           [(ffin_v, vsrc, _MLP[1], _MLP[0])], eps=eps)
-        with section("block.audio_norm"):
-            residual_norm(ax, a_text, tgate_a, _TEXT_Q[2], ax,
-                          [(ffin_a, asrc, _MLP[1], _MLP[0])], eps=eps)
-        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            with section("block.audio_norm"):
+                residual_norm(ax, a_text, tgate_a, _TEXT_Q[2], ax,
+                              [(ffin_a, asrc, _MLP[1], _MLP[0])], eps=eps)
 
     # ── FFNs (kv_cache.py:2600-2640)
     with torch.cuda.stream(side):
@@ -557,6 +624,10 @@ class BlockWeights(torch.nn.Module):
 
 def fuse_block_weights(block) -> int:
     """``fuse_qkv_weights`` on the block's self-attention modules (one
-    projection GEMM per self-attention call); returns how many were fused."""
-    from .attention import fuse_qkv_weights
-    return sum(bool(fuse_qkv_weights(a)) for a in (block.attn1, block.audio_attn1))
+    projection GEMM per self-attention call) and ``fuse_kv_weights`` on the
+    A2V / V2A modules (one GEMM for the keys and values of each); returns how
+    many modules were fused."""
+    from .attention import fuse_kv_weights, fuse_qkv_weights
+    n = sum(bool(fuse_qkv_weights(a)) for a in (block.attn1, block.audio_attn1))
+    return n + sum(bool(fuse_kv_weights(a))
+                   for a in (block.audio_to_video_attn, block.video_to_audio_attn))

@@ -196,13 +196,14 @@ def _output(x: Tensor, table: Tensor, emb2: Tensor, proj: torch.nn.Linear, frame
 
 def model_forward(model: CausalModelWeights, video_tokens: Tensor, audio_tokens: Tensor,
                   cond: Conditioning, cache: KVCache, kv_cache_only: bool = False,
-                  video_token_offset: int = 0):
+                  video_token_offset: int = 0, overlap_audio: bool = True):
     """One forward over a chunk: ``video_tokens [1, Lv_local, C]`` (this rank's
     tokens of the chunk's patchified latents), ``audio_tokens [1, La, C]``
     (all of them).  Returns ``(video_out, audio_out, new_cache)`` with
     ``new_cache`` holding the chunk's K/V appended to every field (the denoise
     forwards drop it, the commit forward keeps it: model_runtime.py:847-895,
-    model.py:88-129); with ``kv_cache_only`` the outputs are None."""
+    model.py:88-129); with ``kv_cache_only`` the outputs are None.
+    ``overlap_audio``: run each block's audio chain on a second stream."""
     cfg = model.cfg
     fs = cfg.frame_tokens
     vpe, ape, vcpe, acpe = cond.pe
@@ -219,7 +220,7 @@ def model_forward(model: CausalModelWeights, video_tokens: Tensor, audio_tokens:
             cond.video_cross_gate, cond.audio_cross_ss, cond.audio_cross_gate, None, None,
             None, None, cache.layers[i], layer_idx=i, video_frame_seqlen=fs,
             audio_frame_seqlen=1, video_token_offset=video_token_offset,
-            audio_replicated=sp)
+            audio_replicated=sp, overlap_audio=overlap_audio)
         layers.append(lc)
     new_cache = KVCache(layers=layers)
     if hasattr(cache, "segments"):

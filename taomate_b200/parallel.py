@@ -433,8 +433,15 @@ class PeerExchange:
     * ``out``: ``[B, S_loc, H, D]`` — this rank's tokens for all heads; rank
       g's attention kernel stores heads ``g * H/sp ...`` of them
       (all_to_all.py:154-173).
+    * ``gather`` (optional, ``gather_bytes`` > 0): two buffers of
+      ``gather_bytes`` for small all-gathers (the V2A partial results under
+      sequence parallelism): rank g's part sits at ``g * part_bytes``; a rank
+      copies its part into every peer's buffer and runs the handshake of
+      slot 2 (:meth:`all_gather_parts`).  Consecutive layers use the two
+      buffers in turn, so a rank that runs ahead never overwrites parts a
+      slower peer is still merging.
     * flags and device epoch counters for the handshakes (slot 0: seq->head,
-      slot 1: head->seq).
+      slot 1: head->seq, slot 2: gather).
 
     The buffers are reused by every call: the returned Q/K/V/out are views
     that the next call overwrites (``attention_with_cache`` copies the new K/V
@@ -443,7 +450,7 @@ class PeerExchange:
     """
 
     def __init__(self, group, sp_size: int, rank: int, batch: int, tokens_local: int,
-                 heads: int, dim_head: int, device: torch.device):
+                 heads: int, dim_head: int, device: torch.device, gather_bytes: int = 0):
         if sp_size < 2 or sp_size > 8 or heads % sp_size:
             raise ValueError(f"peer exchange needs 2..8 ranks dividing {heads} heads")
         lib = _lib.load()
@@ -457,6 +464,9 @@ class PeerExchange:
             "out": batch * tokens_local * heads * dim_head * el,
             "flags": int(lib.tm_peer_flag_bytes()),
         }
+        self.gather_bytes = (int(gather_bytes) + 255) // 256 * 256
+        if self.gather_bytes > 0:
+            sizes["gather"] = 2 * self.gather_bytes
         self._own: Dict[str, int] = {}
         self._opened = []
         handles = {}
@@ -490,6 +500,42 @@ class PeerExchange:
             sp_size, batch, tokens_local, 3, self.Hl, dim_head)
         self.out = _DevBuffer(self._own["out"], sizes["out"], self.device).tensor.view(
             batch, tokens_local, heads, dim_head)
+        self.gather = None
+        if self.gather_bytes:
+            self.gather = _DevBuffer(self._own["gather"], sizes["gather"],
+                                     self.device).tensor.view(torch.uint8)
+
+    def gather_buffer(self, index: int, part_bytes: int) -> Optional[torch.Tensor]:
+        """Gather buffer ``index % 2`` as a uint8 tensor of ``sp * part_bytes``
+        bytes (None when the parts do not fit)."""
+        n = self.sp * int(part_bytes)
+        if self.gather is None or n > self.gather_bytes or part_bytes % 16:
+            return None
+        off = (index % 2) * self.gather_bytes
+        return self.gather[off:off + n]
+
+    def all_gather_parts(self, buf: torch.Tensor, part_bytes: int) -> None:
+        """Copy this rank's part of ``buf`` (a :meth:`gather_buffer` view,
+        already written) into the same place of every peer's buffer over
+        NVLink, then the slot-2 handshake: afterwards ``buf`` holds every
+        rank's part."""
+        base = self._own["gather"]
+        off = buf.data_ptr() - base + self.rank * part_bytes
+        if off < 0 or off + part_bytes > 2 * self.gather_bytes:
+            raise ValueError("not a view of this exchange's gather buffers")
+        spans = (_lib.CopySpan * max(1, self.sp - 1))()
+        i = 0
+        for g in range(self.sp):
+            if g == self.rank:
+                continue
+            spans[i].src, spans[i].dst, spans[i].rows = base + off, self.peers["gather"][g] + off, 1
+            spans[i].src_row_stride = spans[i].dst_row_stride = part_bytes
+            i += 1
+        stream = _lib.stream_ptr(self.device)
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.tm_copy_rows(spans, i, part_bytes, stream), "gather copy")
+            _lib.launched()
+        self.exchange(2)
 
     def fits(self, B: int, L: int, H: int, D: int) -> bool:
         return (B, L, H, D) == (self.B, self.S_loc, self.H, self.D)
@@ -518,10 +564,12 @@ _PEER: Optional[PeerExchange] = None
 
 
 def init_peer_exchange(batch: int, tokens_local: int, heads: int, dim_head: int,
-                       device=None) -> Optional[PeerExchange]:
+                       device=None, gather_bytes: int = 0) -> Optional[PeerExchange]:
     """Map NVLink receive buffers for ``attention_with_cache``'s exchanges on
     the SP group (collective over the group; call after :func:`init_sp_mesh`
-    on every rank).  Calls whose shapes differ keep using NCCL."""
+    on every rank).  Calls whose shapes differ keep using NCCL.
+    ``gather_bytes``: size of each of the two gather buffers of the split-key
+    V2A (``taomate_b200.block.v2a_gather_bytes``); 0 keeps it on NCCL."""
     global _PEER
     if not is_sp_enabled():
         return None
@@ -529,7 +577,7 @@ def init_peer_exchange(batch: int, tokens_local: int, heads: int, dim_head: int,
         _PEER.close()
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
     _PEER = PeerExchange(_SP_GROUP, _SP_SIZE, _SP_RANK, batch, tokens_local, heads, dim_head,
-                         dev)
+                         dev, gather_bytes=gather_bytes)
     return _PEER
 
 

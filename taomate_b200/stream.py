@@ -78,7 +78,7 @@ class _Forward:
         with torch.no_grad():
             self.out_v, self.out_a, new = self.graph.capture(
                 model_forward, runner.model, self.v, self.a, scond, cache,
-                video_token_offset=off)
+                video_token_offset=off, overlap_audio=runner.overlap_audio)
         # the chunk tensors only: views of ``new`` would keep capture-time slots referenced
         self.chunks = [[last_chunk(getattr(lay, kf)) for kf, _ in FIELD_PAIRS]
                        for lay in new.layers]
@@ -90,13 +90,15 @@ class _Forward:
 class StreamRunner:
     """Runs blocks of one stream on this rank.  ``sp``/``rank``: the sequence
     parallel layout (video tokens split, audio replicated).  ``max_graphs``:
-    captured forward layouts kept (least recently used dropped first)."""
+    captured forward layouts kept (least recently used dropped first).
+    ``overlap_audio``: each block's audio chain on a second stream."""
 
     def __init__(self, model: CausalModelWeights, device, sp: int = 1, rank: int = 0,
                  graphed: bool = True, evict_from_block: int = 0, slots: int = 6,
-                 max_graphs: int = 6):
+                 max_graphs: int = 6, overlap_audio: bool = True):
         self.model, self.cfg, self.dev = model, model.cfg, torch.device(device)
         self.sp, self.rank, self.graphed = sp, rank, graphed
+        self.overlap_audio = overlap_audio
         self.evict_from_block = evict_from_block
         cfg = self.cfg
         ff, fa, _, _ = block_geometry(0, cfg)
@@ -211,7 +213,8 @@ class StreamRunner:
                     pe, off = self._pe(k)
                     _, _, rebuilt = model_forward(self.model, v, a, self._cond(conds[k], pe),
                                                   rebuilt, kv_cache_only=True,
-                                                  video_token_offset=off)
+                                                  video_token_offset=off,
+                                                  overlap_audio=self.overlap_audio)
                     self._warm = True
                 flush_many([getattr(lay, kf) for lay in rebuilt.layers for kf, _ in FIELD_PAIRS])
         self.cache = replace_modal_fields(self.cache, rebuilt)
@@ -248,12 +251,14 @@ class StreamRunner:
         with torch.no_grad():
             for fwd in range(3):
                 vo, ao, _ = model_forward(self.model, x_v, x_a, self._cond(conds[fwd], pe),
-                                          self.cache, video_token_offset=off)
+                                          self.cache, video_token_offset=off,
+                                          overlap_audio=self.overlap_audio)
                 dt = SIGMAS[fwd + 1] - SIGMAS[fwd]
                 x_v = torch.add(x_v, vo, alpha=dt)  # the graph path's update, same rounding
                 x_a = torch.add(x_a, ao, alpha=dt)
             _, _, new = model_forward(self.model, x_v, x_a, self._cond(conds[3], pe), self.cache,
-                                      kv_cache_only=True, video_token_offset=off)
+                                      kv_cache_only=True, video_token_offset=off,
+                                      overlap_audio=self.overlap_audio)
         self._warm = True
         self._commit(new, (x_v, x_a))
         return x_v, x_a

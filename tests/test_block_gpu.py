@@ -50,7 +50,8 @@ def _setup(d, arena=False, fused=False):
                        c["audio_heads"], c["audio_dim_head"], device=DEV, std=None)
     blk.load_state_dict({k: torch.from_numpy(v) for k, v in d["params"].items()}, strict=True)
     if fused:
-        assert tm.block.fuse_block_weights(blk) == 2
+        # QKV of the two self-attentions, K/V of A2V and V2A
+        assert tm.block.fuse_block_weights(blk) == 4
     bf = lambda a: torch.from_numpy(a).to(DEV, torch.bfloat16)[None]
     x = {k: bf(v) for k, v in d["x"].items()}
     Hv, dv, Ha, da = c["video_heads"], c["video_dim_head"], c["audio_heads"], c["audio_dim_head"]

@@ -73,7 +73,9 @@ def _worker(rank, world, port, outdir):
                 ck[:, :, hs].contiguous(), cv[:, :, hs].contiguous())
         # the same calls with the exchanges fused into the kernels' NVLink stores,
         # twice in a row (the second on other inputs: buffers and flag epochs reused)
-        P.init_peer_exchange(1, sl, heads, dim_head)
+        from taomate_b200.block import v2a_gather_bytes
+        P.init_peer_exchange(1, sl, heads, dim_head,
+                             gather_bytes=v2a_gather_bytes(16, 4, 64, world))
         x2 = torch.randn(1, lq, hidden, device=dev, generator=g).to(torch.bfloat16)
         with torch.no_grad():
             out_p, nk_p, nv_p = tm.attention_with_cache(
@@ -141,15 +143,21 @@ def _worker(rank, world, port, outdir):
             bv, ba, bc = tm.block_forward_with_cache(
                 blk, vx[:, ts].contiguous(), ax,
                 **bargs(rope_tables(cfg, frames, 16, 3, 26, dev, ts), rank * sl, True, True))
+            # V2A parts gathered over NVLink above; the same block with every
+            # exchange through NCCL
+            P.close_peer_exchange()
+            nv_, na_, _ = tm.block_forward_with_cache(
+                blk, vx[:, ts].contiguous(), ax,
+                **bargs(rope_tables(cfg, frames, 16, 3, 26, dev, ts), rank * sl, True, True))
         torch.cuda.synchronize()
         code = ctypes.c_int(0)
         assert _lib.load().tm_device_error(ctypes.byref(code)) == 0 and code.value == 0
-        P.close_peer_exchange()
         f = lambda t: t.float().cpu().numpy()
         np.savez(os.path.join(outdir, f"b{rank}.npz"), vx=f(bv), ref_vx=f(rv[:, ts]), ax=f(ba),
                  ref_ax=f(ra), vs_k=f(bc.video_self_k[:, lc:]), ref_vs_k=f(rc.video_self_k[:, lc:, hs]),
                  v2a_k=f(bc.v2a_k[:, lc // world:]), ref_v2a_k=f(rc.v2a_k[:, lc:][:, ts]),
-                 a2v_k=f(bc.a2v_k[:, 32:]), ref_a2v_k=f(rc.a2v_k[:, 32:]))
+                 a2v_k=f(bc.a2v_k[:, 32:]), ref_a2v_k=f(rc.a2v_k[:, 32:]),
+                 vx_nccl=f(nv_), ax_nccl=f(na_))
         f = lambda t: t.float().cpu().numpy()
         np.savez(os.path.join(outdir, f"r{rank}.npz"), out=f(out), ref_out=f(ref_out[:, ts]),
                  k=f(nk), ref_k=f(ref_k[:, :, hs]), v=f(nv), ref_v=f(ref_v[:, :, hs]),
@@ -197,3 +205,5 @@ def test_ulysses_sp_matches_single_gpu(tmp_path, world):
         # V2A cache: this rank's video tokens, all heads
         assert _rel_l2(b["v2a_k"], b["ref_v2a_k"]) < 5e-3
         assert _rel_l2(b["a2v_k"], b["ref_a2v_k"]) < 5e-3
+        # NVLink exchanges and gathers against NCCL: the same arithmetic
+        assert _rel_l2(b["vx"], b["vx_nccl"]) < 1e-3 and _rel_l2(b["ax"], b["ax_nccl"]) < 1e-3
