@@ -79,9 +79,11 @@ def parse():
                     help="c4: the 48-block audio-video step (headline); attention: the video "
                          "self-attention step alone; both: c4 headline + attention as an extra key")
     ap.add_argument("--kernel-case", choices=["attention", "norm_rope", "kv_append",
-                                              "residual_norm"], default=None,
+                                              "residual_norm", "linear"], default=None,
                     help="time one kernel in isolation at C2 shapes (profiling target)")
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--rows", type=int, default=144,
+                    help="--kernel-case linear: token rows (1152 / G video, 25 audio)")
     ap.add_argument("--heads", type=int, default=None,
                     help="--kernel-case attention: heads per GPU (32 / sequence-parallel ranks)")
     ap.add_argument("--cached", type=int, default=None,
@@ -850,8 +852,13 @@ def c5_longform(args, dev, rank, world, local):
     segment, whose K/V refresh re-prefills the retained blocks (sigma = 0
     kv_cache_only forwards, runtime.py:386-470) from segment 1 on; no eviction
     inside the first window, then sink + 2 newest after every block, and at
-    every window end.  Timed as a whole on the device (max over ranks),
-    including the eager first window, the graph capture and the refreshes."""
+    every window end.  Timed as a whole on the device (max over ranks): every
+    block and every refresh of the 60 s stream.  Before it, a warm-up stream
+    (the first window, one refresh, one block) captures the CUDA graphs of
+    every cache layout the stream meets, as a service does once at start;
+    the runner is then reset (same arenas, empty cache) and the timed stream
+    replays them from its first block (``graph_captures_timed`` counts any
+    capture inside the timed region)."""
     import torch
     import torch.distributed as dist
     from taomate_b200 import _lib
@@ -877,6 +884,19 @@ def c5_longform(args, dev, rank, world, local):
 
     runner = StreamRunner(model, dev, sp=world, rank=rank, graphed=not args.eager,
                           evict_from_block=per, overlap_audio=not args.serial_audio)
+    # warm-up stream: window 0, a prompt change with its refresh, one block of window 1
+    warm_in = [block_inputs(k) for k in range(per + 1)]
+    runner.set_prompt(prompts[0].video_ctx, prompts[0].audio_ctx)
+    for k in range(per):
+        runner.run_block(*warm_in[k])
+    runner.end_segment()
+    runner.set_prompt(prompts[1 % segs].video_ctx, prompts[1 % segs].audio_ctx)
+    runner.refresh({int(sg["block_idx"]): zero[block_geometry(int(sg["block_idx"]), cfg)[0]]
+                    for sg in runner.cache.segments})
+    runner.run_block(*warm_in[per])
+    del warm_in
+    runner.reset()
+    captures0 = runner.captures
     inputs = [block_inputs(k) for k in range(segs * per)]
     torch.cuda.synchronize()
     if world > 1:
@@ -913,7 +933,7 @@ def c5_longform(args, dev, rank, world, local):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, derr = float(t[0].item()), int(t[1].item())
     captured = runner.graph is not None
-    captures = runner.captures
+    captures = runner.captures - captures0
     runner.release()
     del model
     torch.cuda.empty_cache()
@@ -923,7 +943,7 @@ def c5_longform(args, dev, rank, world, local):
             "blocks": segs * per, "latent_frames": frames, "video_seconds": video_s,
             "wall_ms": ms, "realtime_factor": video_s / (ms / 1e3),
             "refreshes": runner.refreshes, "graph_captured": captured,
-            "graph_captures": captures,
+            "graph_captures_timed": captures,
             "kv_cache_bytes_per_gpu": live, "kv_cache_peak_bytes_per_gpu": peak_cache,
             "kv_arena_bytes_per_gpu": arena, "clocks": clocks, "device_error": derr,
             "config": {"workload": "C5: 60 s long-form stream", "segments": segs,
@@ -1141,6 +1161,8 @@ def run_kernel_case(args):
     Lq = Q_FRAMES * FRAME_TOKENS
     Lc = args.cached or (ANCHOR_FRAMES + WINDOW_FRAMES) * FRAME_TOKENS
     rnd = lambda *s: torch.randn(*s, device=dev, generator=g).to(torch.bfloat16)
+    if args.kernel_case == "linear":
+        return run_linear_case(args, dev, rnd)
     if args.kernel_case == "attention":
         Hk = args.heads or HEADS
         q = rnd(1, Lq, Hk, DIM_HEAD)
@@ -1202,6 +1224,52 @@ def run_kernel_case(args):
                       "cached": Lc,
                       "median_ms": med, "min_ms": ms[0],
                       "achieved": work / (med * 1e-3), "unit": unit}), flush=True)
+
+
+def run_linear_case(args, dev, rnd):
+    """cuBLAS (torch F.linear, bias included) at the block's weight shapes and
+    ``--rows`` token rows, as the captured step runs them: one CUDA graph of
+    consecutive calls over rotating weight copies (more bytes than L2 holds),
+    so launch gaps and L2 reuse match the step.  Prints one line per shape
+    with the time per call and the weight-read floor at the measured HBM
+    bandwidth."""
+    import torch
+    import torch.nn.functional as F
+    peaks, kind = measured_peaks()
+    hbm = float(peaks["hbm_gbs"]) * 1e9
+    shapes = {"video_qkv": (4096, 12288), "video_out": (4096, 4096), "ff1": (4096, 16384),
+              "ff2": (16384, 4096), "a2v_q": (4096, 2048), "v2a_kv": (4096, 4096),
+              "audio_qkv": (2048, 6144), "audio_out": (2048, 2048), "audio_ff1": (2048, 8192),
+              "audio_ff2": (8192, 2048)}
+    M = args.rows
+    for name, (K, N) in shapes.items():
+        copies = min(16, max(2, int(4 * 134e6 // (K * N * 2)) + 1))
+        ws = [rnd(N, K) * 0.02 for _ in range(copies)]
+        b = rnd(N) * 0.1
+        x = rnd(M, K)
+        for i in range(copies):
+            F.linear(x, ws[i], b)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(copies):
+                F.linear(x, ws[i], b)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (args.reps * copies)
+        floor = K * N * 2 / hbm * 1e6
+        print(json.dumps({"kernel_case": "linear", "shape": name, "rows": M, "K": K, "N": N,
+                          "us_per_call": round(us, 2), "weight_floor_us": round(floor, 2),
+                          "floor_source": f"{kind} hbm_gbs",
+                          "tflops": round(2 * M * K * N / us / 1e6, 1)}), flush=True)
+        del ws
+        torch.cuda.empty_cache()
 
 
 def main():

@@ -26,6 +26,7 @@ them per prompt).
 
 from __future__ import annotations
 
+import gc
 import time
 from collections import OrderedDict
 from dataclasses import dataclass, fields
@@ -59,6 +60,17 @@ def block_geometry(k: int, cfg: StreamConfig, first_frames: int = 4, frames: int
     if k == 0:
         return first_frames, audio_first, 0, 0
     return frames, audio, first_frames + frames * (k - 1), audio_first + audio * (k - 1)
+
+
+def _empty_cache(cache: KVCache) -> KVCache:
+    """A cache with every field empty, on the same arenas as ``cache``."""
+    layers = []
+    for lay in cache.layers:
+        kw = {}
+        for kf, vf in FIELD_PAIRS:
+            kw[kf], kw[vf] = arena_pair(getattr(lay, kf).arena)
+        layers.append(LayerKVCache(**kw))
+    return attach_segments(KVCache(layers=layers), [])
 
 
 class _Forward:
@@ -115,6 +127,24 @@ class StreamRunner:
         self.refreshes = 0
         self.host_ms = {}  # host time of the replayed blocks, by phase
         self.host_blocks = 0
+
+    def reset(self) -> None:
+        """Start a new stream on the same arenas: every cache field empty (all
+        slots free), no retained latents, block 0.  The captured forwards and
+        the text graph stay: they depend only on the cache layout, so a new
+        stream replays them from its first block (a service captures them
+        once, in a warm-up stream)."""
+        arenas = [(i, kf, getattr(lay, kf).arena) for i, lay in enumerate(self.cache.layers)
+                  for kf, _ in FIELD_PAIRS]
+        self.cache = _empty_cache(self.cache)
+        self.latents = {}
+        self.block = 0
+        gc.collect()  # views of the old stream that sit in reference cycles release their slots
+        busy = [(i, kf, [s for s, r in enumerate(a.refs) if r]) for i, kf, a in arenas
+                if any(a.refs)]
+        if busy:
+            raise RuntimeError(f"arena slots still referenced after reset (layer, field, "
+                               f"slots): {busy[:4]}")
 
     @property
     def graph(self) -> Optional[AttentionGraph]:
@@ -190,13 +220,7 @@ class StreamRunner:
         segs = cache_segments(self.cache)
         if not segs:
             raise RuntimeError("The retained cache has no block metadata.")
-        layers = []
-        for lay in self.cache.layers:
-            kw = {}
-            for kf, vf in FIELD_PAIRS:
-                kw[kf], kw[vf] = arena_pair(getattr(lay, kf).arena)
-            layers.append(LayerKVCache(**kw))
-        rebuilt = KVCache(layers=layers)
+        rebuilt = _empty_cache(self.cache)
         with torch.no_grad():
             for seg in segs:
                 k = int(seg["block_idx"])

@@ -161,3 +161,49 @@ def test_longform_refresh_graph_equals_eager():
     for i, ((ev, ea), (gv, ga)) in enumerate(zip(eo, go)):
         assert torch.equal(ev, gv), f"video output of block {i}"
         assert torch.equal(ea, ga), f"audio output of block {i}"
+
+
+def test_reset_stream_replays_captured_layouts():
+    """A second stream on the same runner (``reset``: same arenas, empty
+    cache) replays the graphs the first stream captured from its first block
+    on, captures nothing, and gives the first stream's bits for the same
+    inputs."""
+    from taomate_b200.model import synthetic_conditioning
+    from taomate_b200.stream import StreamRunner, block_geometry
+    cfg, model = _small()
+    runner = StreamRunner(model, DEV, graphed=True, evict_from_block=5)
+
+    def stream():
+        gen = torch.Generator(device=DEV).manual_seed(8)
+        prompts = [synthetic_conditioning(cfg, 3, 25, DEV, gen) for _ in range(2)]
+        zero = {4: synthetic_conditioning(cfg, 4, 26, DEV, gen),
+                3: synthetic_conditioning(cfg, 3, 25, DEV, gen)}
+        outs = []
+        for s in range(2):
+            runner.set_prompt(prompts[s].video_ctx, prompts[s].audio_ctx)
+            if s > 0:
+                runner.refresh({int(g["block_idx"]): zero[block_geometry(int(g["block_idx"]),
+                                                                         cfg)[0]]
+                                for g in runner.cache.segments})
+            for b in range(5 if s == 0 else 2):
+                F_, La, _, _ = block_geometry(s * 5 + b, cfg)
+                v = torch.randn(1, F_ * cfg.frame_tokens, cfg.in_channels, device=DEV,
+                                generator=gen).to(torch.bfloat16)
+                a = torch.randn(1, La, cfg.in_channels, device=DEV,
+                                generator=gen).to(torch.bfloat16)
+                conds = [synthetic_conditioning(cfg, F_, La, DEV, gen) for _ in range(4)]
+                outs.append(tuple(t.clone() for t in runner.run_block(v, a, conds)))
+            runner.end_segment()
+        torch.cuda.synchronize()
+        return outs
+
+    first = stream()
+    n = runner.captures
+    assert n == 5
+    runner.reset()
+    second = stream()
+    assert runner.captures == n
+    for i, ((v1, a1), (v2, a2)) in enumerate(zip(first, second)):
+        assert torch.equal(v1, v2), f"video output of block {i}"
+        assert torch.equal(a1, a2), f"audio output of block {i}"
+    runner.release()
