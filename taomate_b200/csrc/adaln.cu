@@ -68,24 +68,35 @@ __device__ __forceinline__ uint4 f32_to_bf8(const float* f) {
   return u;
 }
 
-// value of parameter p at columns c..c+7 for token row (b, t)
-__device__ __forceinline__ void param8(const Src& s, int p, int D, int b, int t, int c,
-                                       float* out) {
+// The parameter rows of one token row (b, t): the table and this token's
+// timestep row (row (t + offset) / div, computed once per CTA).
+struct Row {
+  const __nv_bfloat16* table;
+  const __nv_bfloat16* ts;
+};
+
+__device__ __forceinline__ Row param_row(const Src& s, int b, int t) {
+  Row r{s.table, nullptr};
+  if (s.ts) {
+    const int row = (t + s.ts_off) / s.ts_div;  // 32-bit: token and frame indices fit
+    r.ts = s.ts + b * s.ts_bs + static_cast<int64_t>(row) * s.ts_rs;
+  }
+  return r;
+}
+
+// value of parameter p at columns c..c+7: table[p] + ts_row[p]
+__device__ __forceinline__ void param8(const Row& s, int p, int D, int c, float* out) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) out[i] = 0.f;
   float tmp[8];
+  const int64_t off = static_cast<int64_t>(p) * D + c;
   if (s.table) {
-    bf8_to_f32(__ldg(reinterpret_cast<const uint4*>(s.table + static_cast<int64_t>(p) * D + c)),
-               tmp);
+    bf8_to_f32(__ldg(reinterpret_cast<const uint4*>(s.table + off)), tmp);
 #pragma unroll
     for (int i = 0; i < 8; ++i) out[i] += tmp[i];
   }
   if (s.ts) {
-    const int row = (t + s.ts_off) / s.ts_div;  // 32-bit: token and frame indices fit
-    bf8_to_f32(__ldg(reinterpret_cast<const uint4*>(s.ts + b * s.ts_bs +
-                                                    static_cast<int64_t>(row) * s.ts_rs +
-                                                    static_cast<int64_t>(p) * D + c)),
-               tmp);
+    bf8_to_f32(__ldg(reinterpret_cast<const uint4*>(s.ts + off)), tmp);
 #pragma unroll
     for (int i = 0; i < 8; ++i) out[i] += tmp[i];
   }
@@ -114,6 +125,7 @@ __global__ void __launch_bounds__(NT, 4) residual_norm_kernel(const __grid_const
   const int row = blockIdx.x;
   const int b = row / p.L, t = row - b * p.L;
   const int D = p.D;
+  const Row gate_row = param_row(p.gate, b, t);
   float v[CH][8];
 #pragma unroll
   for (int j = 0; j < CH; ++j) {
@@ -128,7 +140,7 @@ __global__ void __launch_bounds__(NT, 4) residual_norm_kernel(const __grid_const
       bf8_to_f32(__ldg(reinterpret_cast<const uint4*>(p.y + b * p.y_bs + t * p.y_rs + c)), y);
       if (p.gate_idx >= 0) {
         float g[8];
-        param8(p.gate, p.gate_idx, D, b, t, c, g);
+        param8(gate_row, p.gate_idx, D, c, g);
 #pragma unroll
         for (int i = 0; i < 8; ++i) y[i] *= g[i];
       }
@@ -161,6 +173,7 @@ __global__ void __launch_bounds__(NT, 4) residual_norm_kernel(const __grid_const
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     if (k >= p.n_out) break;
+    const Row mod_row = param_row(p.mod[k], b, t);
 #pragma unroll
     for (int j = 0; j < CH; ++j) {
       const int c = (j * NT + threadIdx.x) * 8;
@@ -169,8 +182,8 @@ __global__ void __launch_bounds__(NT, 4) residual_norm_kernel(const __grid_const
       for (int i = 0; i < 8; ++i) o[i] = (v[j][i] - mean) * inv;
       if (p.scale_idx[k] >= 0) {
         float sc[8], sh[8];
-        param8(p.mod[k], p.scale_idx[k], D, b, t, c, sc);
-        param8(p.mod[k], p.shift_idx[k], D, b, t, c, sh);
+        param8(mod_row, p.scale_idx[k], D, c, sc);
+        param8(mod_row, p.shift_idx[k], D, c, sh);
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[i] = o[i] * (1.f + sc[i]) + sh[i];
       }
