@@ -21,8 +21,9 @@ Sequence parallelism (one process per GPU): the video stream is split by
 tokens (each rank holds 1152 / G of a 3-frame chunk and 32 / G heads of the
 video self-attention cache, as the reference lays it out, kv_cache.py:
 331-339); the 25-token audio stream is replicated (``audio_replicated`` of
-``block_forward_with_cache``), so only the video self-attention's two
-exchanges and V2A's one all-gather cross NVLink per block.
+``block_forward_with_cache``), so per layer only the video self-attention's
+two exchanges and the gather of V2A's partial results (~0.2 MB per rank)
+cross NVLink; each rank's V2A cache holds its own video tokens.
 """
 
 from __future__ import annotations
