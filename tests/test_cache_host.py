@@ -167,3 +167,26 @@ def test_replace_modal_fields_keeps_video_self():
     assert C.cache_segments(out) == segs
     with pytest.raises(RuntimeError):
         C.replace_modal_fields(cache, KVCache(layers=[]))
+
+
+def test_retention_slices_a_per_rank_v2a_cache_by_its_share():
+    """Under sequence parallelism each rank's V2A cache holds its own 1/G of
+    every segment's video tokens (the split-key V2A); retention keeps the
+    same segments of it as of the full-sequence fields."""
+    a = _arena(n_slots=8, slot_rows=24)
+    b = _arena(n_slots=8, slot_rows=12)
+    lens = [24, 18, 18, 18, 18]
+    vk, vv = _pair_with(a, lens)
+    sk, sv = _pair_with(b, [n // 2 for n in lens])  # G = 2
+    layer = LayerKVCache(video_self_k=vk, video_self_v=vv, v2a_k=sk, v2a_v=sv)
+    segs = [{"block_idx": i, "video_tokens": n, "audio_tokens": 0} for i, n in enumerate(lens)]
+    out = C.retain_streaming_context(C.attach_segments(KVCache(layers=[layer]), segs))
+    lay = out.layers[0]
+    assert [e[0] for e in lay.video_self_k._state.entries] == [0, 3, 4]
+    assert [e[0] for e in lay.v2a_k._state.entries] == [0, 3, 4]
+    assert lay.v2a_k.shape[1] == (24 + 18 + 18) // 2 and lay.video_self_k.shape[1] == 60
+    # a field whose rows are not a whole share of the tokens is refused
+    ck, cv = _pair_with(_arena(n_slots=8, slot_rows=24), [7, 5, 5, 5, 5])
+    bad = LayerKVCache(video_self_k=vk, video_self_v=vv, v2a_k=ck, v2a_v=cv)
+    with pytest.raises(ValueError):
+        C.retain_streaming_context(C.attach_segments(KVCache(layers=[bad]), segs))
