@@ -16,8 +16,8 @@ What runs where:
     per token row that adds the previous sublayer's gated output into the
     residual stream and writes the next sublayer's modulated input (up to two
     of them: the cross-modal pair reads two modulations of one norm);
-  * FFN: the two linears through cuBLAS (torch), the tanh GELU in
-    ``tm_gelu_tanh`` in place.
+  * FFN: the two linears through cuBLAS (torch), the tanh GELU in the
+    first one's epilogue (``tm_gelu_tanh`` in place when it has no bias).
 
 AdaLN parameters come as the reference passes them (per token, ``[B, L, n *
 D]``) or per frame (``[B, F, n * D]`` with ``video_frame_seqlen`` /
@@ -159,10 +159,20 @@ def gelu_tanh_(x: Tensor) -> Tensor:
 
 def feed_forward(ff, x: Tensor) -> Tensor:
     """``FeedForward`` (ltx_causal/transformer/compat.py:47-70): Linear ->
-    tanh GELU -> Linear; the linears through cuBLAS, the GELU in place."""
+    tanh GELU -> Linear, both linears through cuBLAS.  With a bias the GELU
+    runs in the first GEMM's epilogue (cuBLASLt GELU_BIAS, the tanh form, on
+    the fp32 accumulator: one bf16 rounding instead of two, and the hidden
+    rows are written once instead of written, read and written again);
+    without one, ``tm_gelu_tanh`` in place."""
     proj = ff.net[0].proj
-    h = F.linear(x, proj.weight, proj.bias)
-    gelu_tanh_(h)
+    x2 = x.reshape(-1, x.shape[-1])
+    if proj.bias is not None and x2.is_contiguous() and x2.shape[0] > 1 and \
+            proj.bias.dtype == x.dtype == proj.weight.dtype:
+        h = torch._addmm_activation(proj.bias, x2, proj.weight.t(), use_gelu=True)
+        h = h.view(*x.shape[:-1], h.shape[-1])
+    else:
+        h = F.linear(x, proj.weight, proj.bias)
+        gelu_tanh_(h)
     out = ff.net[2]
     return F.linear(h, out.weight, out.bias)
 

@@ -96,3 +96,48 @@ def test_residual_norm_rows_beyond_one_wave():
     v = x[0].float()
     ref = v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + 1e-6)
     assert _rel(out[0], ref) < 2.5e-3
+
+
+@pytest.mark.parametrize("n", [8, 4096 * 3, 1152 * 16384])
+def test_gelu_tanh_vs_torch(n):
+    """tm_gelu_tanh in place against torch's tanh GELU of the same bf16 input
+    computed in fp32 (one bf16 rounding of the result each)."""
+    from taomate_b200.block import gelu_tanh_
+    g = torch.Generator().manual_seed(n)
+    x = (torch.randn(n, generator=g) * 3).to(DEV, torch.bfloat16)
+    ref = torch.nn.functional.gelu(x.float(), approximate="tanh")
+    gelu_tanh_(x)
+    assert (x.float() - ref).abs().max() <= ref.abs().max() * 2 ** -7
+    assert _rel(x, ref) < 3e-3
+
+
+def test_feed_forward_gelu_epilogue():
+    """The block's FFN (bias + tanh GELU fused into the first GEMM) against an
+    fp64 restatement, and the unfused path (no bias: tm_gelu_tanh) against the
+    same restatement."""
+    from taomate_b200.block import feed_forward
+
+    class _Lin(torch.nn.Module):
+        def __init__(self, w, b):
+            super().__init__()
+            self.weight, self.bias = w, b
+
+    class _FF(torch.nn.Module):
+        def __init__(self, w1, b1, w2, b2):
+            super().__init__()
+            p = torch.nn.Module()
+            p.proj = _Lin(w1, b1)
+            self.net = [p, None, _Lin(w2, b2)]
+
+    g = torch.Generator().manual_seed(7)
+    r_ = lambda *s: torch.randn(*s, generator=g).to(DEV, torch.bfloat16)
+    D, I = 1024, 4096
+    x = r_(1, 300, D)
+    w1, b1, w2, b2 = r_(I, D) * 0.05, r_(I) * 0.05, r_(D, I) * 0.02, r_(D) * 0.02
+    for bias in (True, False):
+        ff = _FF(w1, b1 if bias else None, w2, b2)
+        out = feed_forward(ff, x)
+        h = x.double() @ w1.double().t() + (b1.double() if bias else 0)
+        ref = torch.nn.functional.gelu(h, approximate="tanh") @ w2.double().t() + b2.double()
+        assert out.shape == (1, 300, D)
+        assert _rel(out, ref) < 5e-3
