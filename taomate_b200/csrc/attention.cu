@@ -79,7 +79,8 @@ struct __align__(64) Params {
   float* part_o;          // kv_splits > 1: [kv_splits][B][Lq][H][D] normalised partial outputs
   float2* part_ml;        //                [kv_splits][B][Lq][H] (max * log2 scale, sum)
   const int2* tiles_dev;  // non-null: read the key-tile list from device memory (graph replay)
-  int mode;               // 0: pair CTAs (+ one split CTA for an odd tile); 1: split CTAs only
+  int mode;               // 0: pair CTAs (+ one split CTA for an odd tile); 1: split CTAs only;
+                          // 2: pair CTAs, the odd tiles of heads (h, h + 1) in one CTA
   int kv_splits;          // mode 1: key-tile ranges per query tile
   int partial_only;       // part_o / part_ml belong to the caller: no combine pass
   CUtensorMap tm_q;
@@ -194,16 +195,25 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   const int n = p.n_tiles;
   const int pairs = p.n_qtiles >> 1;
   const bool single = p.mode == 1;
+  // Mode 2: the odd query tile of heads (h, h + 1), h even, in one CTA with one
+  // head per lane; the CTA of head h + 1 has nothing to do.  (With an odd head
+  // count the last head's odd tile stays a split CTA.)
+  const bool odd_tile_cta = !single && cta >= pairs;
+  if (p.mode == 2 && odd_tile_cta && (head & 1)) return;
+  const bool xh = p.mode == 2 && odd_tile_cta && head + 1 < static_cast<int>(gridDim.x);
   const int kvs = single ? p.kv_splits : 1;
   const int sidx = single ? cta % kvs : 0;  // key range of this CTA
-  const bool split = single || cta >= pairs;
+  const bool split = !xh && (single || cta >= pairs);
+  const bool alt = split || xh;  // the lanes take alternate items of the K/V stream
   const int qt0 = single ? cta / kvs : 2 * cta;
   // this CTA's key tiles [kb, kb + nr)
   const int kb = static_cast<int>(static_cast<int64_t>(sidx) * n / kvs);
   const int nr = static_cast<int>(static_cast<int64_t>(sidx + 1) * n / kvs) - kb;
-  // key tiles per lane; split: lane 0 [kb, kb + n0), lane 1 the rest; pair: both all
+  // key tiles per lane; split: lane 0 [kb, kb + n0), lane 1 the rest; pair and
+  // cross-head: both all (cross-head: each its own head's copy of the tiles)
   const int n0 = split ? (nr + 1) >> 1 : nr;
   const int n1 = split ? nr - n0 : nr;
+  const int n_items = xh ? 2 * nr : nr;  // K/V tile loads of this CTA
 
   const uint32_t bar0 = sbase + C::kBarOff;
   const uint32_t b_qfull = bar0;
@@ -221,15 +231,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   float* m1_smem = reinterpret_cast<float*>(smem + C::kMLOff);
   float* l1_smem = m1_smem + BM;
 
-  // stream item -> key tile; lane step -> stream item
+  // stream item -> key tile (and head, cross-head); lane step -> stream item
   const int2* tl = p.tiles_dev ? p.tiles_dev : p.tiles;
   auto tile_of = [&](int g) {
+    if (xh) return kb + (g >> 1);
     return kb + (split ? ((g & 1) ? n0 + (g >> 1) : (g >> 1)) : g);
   };
-  auto item_of = [&](int l, int j) { return split ? 2 * j + l : j; };
+  auto item_of = [&](int l, int j) { return alt ? 2 * j + l : j; };
 
   if (threadIdx.x == 0) {
-    const uint32_t consumers = split ? 1u : 2u;
+    const uint32_t consumers = alt ? 1u : 2u;
     mbar_init(b_qfull, 1);
     for (int s = 0; s < KS; ++s) {
       mbar_init(b_kfull(s), 1);
@@ -280,10 +291,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         for (int t = 0; t < nq; ++t)
           for (int db = 0; db < kDB; ++db)
             tma_load_4d(sbase + C::kQOff + t * C::kQBytes + db * C::kQBlk, &p.tm_q, b_qfull,
-                        db * 64, head, (qt0 + t) * BM, batch);
+                        db * 64, xh ? head + t : head, (xh ? qt0 : qt0 + t) * BM, batch);
       }
       int last = -1;
-      for (int g = 0; g < nr; ++g) {
+      for (int g = 0; g < n_items; ++g) {
         const int s = g % S;
         if (g >= S && !mbar_wait(is_k ? b_kempty(s) : b_vempty(s), ((g / S) - 1) & 1, abort_flag,
                                  p.err))
@@ -295,8 +306,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         const uint32_t dst = sbase + (is_k ? C::kKOff : C::kVOff) + s * C::kKVBytes;
         const CUtensorMap* map = is_k ? &p.tm_k[src] : &p.tm_v[src];
         mbar_arrive_expect_tx(full, C::kKVBytes);
+        const int hd = xh ? head + (g & 1) : head;
         for (int db = 0; db < kDB; ++db)
-          tma_load_4d(dst + db * C::kBlk, map, full, db * 64, head, row, batch);
+          tma_load_4d(dst + db * C::kBlk, map, full, db * 64, hd, row, batch);
         last = g;
       }
       if (*abort_flag) {
@@ -393,7 +405,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     const uint32_t tO = t_lane + C::kOCol + ln * D;
     const int my_n = ln == 0 ? n0 : n1;
     const int tile0 = kb + ((split && ln == 1) ? n0 : 0);
-    const int qi = (split ? qt0 : qt0 + ln) * BM + row;
+    const int qi = (alt ? qt0 : qt0 + ln) * BM + row;
+    const int ohead = xh ? head + ln : head;  // the head this lane's rows belong to
     const float sl = p.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
@@ -551,14 +564,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         }
       } else {
       if (qi < p.Lq) {
-        const float g = gate_of(p.gate, p.gate_bs, p.gate_rs, batch, qi, head);
+        const float g = gate_of(p.gate, p.gate_bs, p.gate_rs, batch, qi, ohead);
         s0 *= g;
         s1 *= g;
       }
       if (!p.stage_out) {
         // every row stays on this GPU: each thread stores its own row
         __nv_bfloat16* orow = out_row(p.out, p.out_bs, p.out_rs, p.rows_per_rank, p.head_base,
-                                      p.out_delta, batch, qi, head, D);
+                                      p.out_delta, batch, qi, ohead, D);
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t o[32], o1[32];
@@ -625,7 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         const int rr = i * kRowsPer + lane_id / kPieces;
         if (qw + rr < p.Lq) {
           __nv_bfloat16* orow = out_row(p.out, p.out_bs, p.out_rs, p.rows_per_rank, p.head_base,
-                                        p.out_delta, batch, qw + rr, head, D);
+                                        p.out_delta, batch, qw + rr, ohead, D);
           *reinterpret_cast<uint4*>(orow + pc * 8) =
               stg[rr * kPieces + (pc ^ (rr & (kPieces - 1)))];
         }
@@ -754,9 +767,11 @@ static int launch(Params& prm, int B, int Lq, int H, cudaStream_t stream) {
   }
   // mode 0: pair CTAs (two query tiles of a head each), then the odd tile's
   // split CTA, head-minor so that every head's pair CTAs launch before any
-  // split CTA.  mode 1: one CTA per (query tile, key range).
+  // split CTA.  mode 2: the same grid; the odd tiles of heads h and h + 1 go
+  // to head h's CTA (head h + 1's returns at once).  mode 1: one CTA per
+  // (query tile, key range).
   const int nq = (Lq + BM - 1) / BM;
-  dim3 grid(H, prm.mode == 0 ? nq / 2 + (nq & 1) : nq * prm.kv_splits, B);
+  dim3 grid(H, prm.mode != 1 ? nq / 2 + (nq & 1) : nq * prm.kv_splits, B);
   attn_fwd_kernel<D><<<grid, kThreads, C::kSmemAlloc, stream>>>(prm);
   int st = check_cuda(cudaGetLastError(), "attention: launch");
   if (st || prm.kv_splits <= 1 || prm.partial_only) return st;
@@ -834,6 +849,17 @@ static Plan make_plan(int B, int Lq, int H, int D, int n_tiles, int64_t ws_bytes
                                         c0 * waves(big + small));
   Plan best{0, 1};
   double best_cost = cost_pair;
+  // mode 2: with an odd tile count, the odd tiles of two heads share one
+  // 2-unit CTA (each lane its own head), so every CTA carries 2 units: one
+  // wave where pair mode spills the odd tiles' CTAs into a second one.
+  if ((nq & 1) && H >= 2) {
+    const int64_t ctas = static_cast<int64_t>(B) * (H * (nq / 2) + (H + 1) / 2);
+    const double cost2 = waves(ctas) * (2.0 + c0);
+    if (cost2 < best_cost - 1e-9) {
+      best_cost = cost2;
+      best = Plan{2, 1};
+    }
+  }
   const int s_max = std::max(1, std::min(32, n_tiles / 2));
   for (int s = 1; s <= s_max; ++s) {
     if (s > 1 && split_ws_bytes(s, B, Lq, H, D) > ws_bytes) break;

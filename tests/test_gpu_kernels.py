@@ -203,6 +203,9 @@ ATTN_SHAPES = [
     (8, 128, 1152, 3456, [(0, 3456)], 1152),
     (4, 128, 1152, 6144, [(0, 384), (1536, 3072)], 1152),
     (1, 64, 25, 0, [], 4608),                            # V2A with one head per GPU
+    # 31 heads x 9 query tiles: the odd tiles of heads (0, 1) ... (28, 29) in
+    # cross-head CTAs, head 30's in a split CTA (124 + 16 CTAs, one wave)
+    (31, 64, 1152, 192, [(0, 192)], 64),
 ]
 
 
@@ -556,14 +559,43 @@ def test_attention_fused_gate(H):
     assert rel_l2(out, ref) < 1.02 * rel_l2(refb, ref) + 1e-4
 
 
+@pytest.mark.parametrize("B,H,D,Lk", [(1, 32, 128, 256), (2, 16, 128, 256), (1, 32, 64, 101),
+                                       (2, 16, 64, 4992)])
+def test_attention_cross_head_odd_tiles(B, H, D, Lk):
+    """9 query tiles per head at B x H = 32: pair mode would need 128 pair
+    CTAs + 32 odd-tile CTAs (two waves on 148 SMs), so the plan puts the odd
+    tiles of heads (h, h + 1) in one CTA, one head per softmax lane, the two
+    heads' K/V tiles alternating through the shared ring.  Text-like (256
+    keys), A2V-like (101 keys) and video-like (4992 keys) key counts, batch 2
+    (pairs never cross a batch), with the per-head gate; against gating the
+    fp32 reference."""
+    from taomate_b200 import flash_attention
+    gen = torch.Generator().manual_seed(41 + B + H + D + Lk)
+    Lq = 1152
+    q = torch.randn(B, Lq, H, D, generator=gen).to(DEV, torch.bfloat16)
+    k = torch.randn(B, Lk, H, D, generator=gen).to(DEV, torch.bfloat16)
+    v = torch.randn(B, Lk, H, D, generator=gen).to(DEV, torch.bfloat16)
+    logits = (torch.randn(B, Lq, H, generator=gen) * 2).to(DEV, torch.bfloat16)
+    out = flash_attention(q, None, None, [], k, v, Lk, gate_logits=logits)
+    g = (2.0 * torch.sigmoid(logits.float()))[..., None]
+    ref = _sdpa_ref(q, [k], [v]) * g
+    refb = _sdpa_bf16(q, [k], [v]).float() * g
+    assert torch.isfinite(out).all()
+    assert rel_l2(out, ref) < 1.02 * rel_l2(refb, ref) + 1e-4
+    for b in range(B):  # each batch entry on its own, same bits
+        ob = flash_attention(q[b:b + 1], None, None, [], k[b:b + 1], v[b:b + 1], Lk,
+                             gate_logits=logits[b:b + 1])
+        assert rel_l2(ob, out[b:b + 1]) < 4e-3
+
+
 @pytest.mark.parametrize("H", [32, 16, 4])
 def test_attention_output_placement_across_rank_buffers(H):
     """The head->seq placement of the fused exchange, on one GPU: query rows
     [r * S, (r + 1) * S) land in "rank" r's buffer [1, S, 2 H, D] at heads
     [H, 2 H), through the per-rank byte offsets (here two local buffers
     instead of a local and a peer-mapped one).  That switches the epilogue to
-    whole-row stores through shared memory (pair CTAs and the odd tile's
-    split CTA at 32 heads, split CTAs at 16, the key-range merge at 4); the
+    whole-row stores through shared memory (pair CTAs and the cross-head
+    odd-tile CTAs at 32 heads, split CTAs at 16, the key-range merge at 4); the
     rows must equal the plain call's bit for bit."""
     from types import SimpleNamespace
     from taomate_b200 import flash_attention
