@@ -372,6 +372,9 @@ def run_reference(args):
         "e2e": {"value": value, "unit": "latent frames/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "cpu_breakdown": cpu_breakdown(),
+        # what this box holds of the reference itself: an offline install of its
+        # tree into baseline/_ref is refused (no setup.py / pyproject.toml)
+        "reference_installed": os.path.isdir(os.path.join(ROOT, "baseline", "_ref")),
     }
     print(json.dumps(line), flush=True)
 
