@@ -301,6 +301,26 @@ TM_API int tm_attention_fwd_ws(const void* q, int64_t q_batch_stride, int64_t q_
 TM_API int64_t tm_attention_workspace_bytes(int B, int Lq, int H, int D, int64_t visible_keys);
 
 /*
+ * No counterpart in the reference: describes this library's launch.
+ *
+ * The work partition tm_attention_fwd / _ws / _noalloc choose for these
+ * shapes on the current device, with `workspace_bytes` of workspace and the
+ * visible keys in one span (each extra span can add one key tile):
+ *   *mode       0: pair CTAs (two 128-row query tiles of a head share every
+ *                  key tile), the odd tile of a head in a split CTA;
+ *               1: split CTAs (one query tile; the two softmax lanes take
+ *                  alternate key tiles), *kv_splits key ranges per query tile
+ *                  merged by a second pass when > 1;
+ *               2: pair CTAs, the odd tiles of heads h and h + 1 in one CTA
+ *                  (one head per softmax lane);
+ *   *kv_splits  key ranges per query tile (1 unless mode 1);
+ *   *ctas       CTAs that do work (one per SM at a time).
+ * Host arithmetic only: no device memory is touched.
+ */
+TM_API int tm_attention_plan(int B, int Lq, int H, int D, int64_t visible_keys,
+                             int64_t workspace_bytes, int* mode, int* kv_splits, int* ctas);
+
+/*
  * Options of tm_attention_fwd_ext (zero-initialise, then set what is used):
  *   device_tiles     key-tile table in device memory (tm_attention_tiles
  *                    layout), as tm_attention_fwd_dev_tiles; NULL: from spans

@@ -102,6 +102,8 @@ _SIGS = {
                                              ctypes.c_int, c_i64]),
     "tm_attention_partial_bytes": (c_i64, [ctypes.c_int] * 5),
     "tm_attention_partial_splits": (ctypes.c_int, [ctypes.c_int] * 4 + [c_i64]),
+    "tm_attention_plan": (ctypes.c_int, [ctypes.c_int] * 4 + [c_i64, c_i64] +
+                          [ctypes.POINTER(ctypes.c_int)] * 3),
     "tm_attention_combine": (ctypes.c_int, [c_vp, ctypes.c_int, c_i64, ctypes.c_int, ctypes.c_int,
                                             ctypes.c_int, ctypes.c_int, ctypes.c_int, c_vp, c_i64,
                                             c_i64, c_vp, c_i64, c_i64, c_vp]),

@@ -160,6 +160,24 @@ def partial_splits(B: int, Lq: int, H: int, D: int, keys: int) -> int:
     return int(_lib.load().tm_attention_partial_splits(B, Lq, H, D, keys))
 
 
+_PLAN_MODES = {0: "pair", 1: "split", 2: "pair+cross-head"}
+
+
+def attention_plan(B: int, Lq: int, H: int, D: int, keys: int,
+                   workspace_bytes: Optional[int] = None) -> dict:
+    """The work partition the attention entry points choose for ``B x Lq``
+    queries and ``H`` heads of dim ``D`` over ``keys`` keys in one span with
+    ``workspace_bytes`` of workspace (None: as much as the plan wants):
+    ``{"mode": "pair" | "split" | "pair+cross-head", "kv_splits": s,
+    "ctas": n}`` (``tm_attention_plan``; host arithmetic, no GPU needed)."""
+    mode, splits, ctas = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    ws = (1 << 62) if workspace_bytes is None else int(workspace_bytes)
+    _lib.check(_lib.load().tm_attention_plan(B, Lq, H, D, int(keys), ws, ctypes.byref(mode),
+                                            ctypes.byref(splits), ctypes.byref(ctas)),
+               "attention_plan")
+    return {"mode": _PLAN_MODES[mode.value], "kv_splits": splits.value, "ctas": ctas.value}
+
+
 def combine_partials(parts: Tensor, n_groups: int, group_bytes: int, splits: int, B: int,
                      Lq: int, H: int, D: int, out: Optional[Tensor] = None,
                      gate_logits: Optional[Tensor] = None) -> Tensor:

@@ -1124,6 +1124,34 @@ extern "C" int64_t tm_attention_workspace_bytes(int B, int Lq, int H, int D,
   return split_ws_bytes(plan.kv_splits, B, Lq, H, D);
 }
 
+extern "C" int tm_attention_plan(int B, int Lq, int H, int D, int64_t visible_keys,
+                                 int64_t workspace_bytes, int* mode, int* kv_splits, int* ctas) {
+  using namespace tmb::attn;
+  if (!mode || !kv_splits || !ctas)
+    return set_error(TM_ERR_INVALID_ARGUMENT, "attention_plan: null output");
+  if (B < 1 || Lq < 1 || H < 1 || visible_keys < 1 || workspace_bytes < 0)
+    return set_error(TM_ERR_INVALID_ARGUMENT, "attention_plan: B=%d Lq=%d H=%d keys=%lld", B,
+                     Lq, H, (long long)visible_keys);
+  if (D != 64 && D != 128) return set_error(TM_ERR_UNSUPPORTED, "attention_plan: head dim %d", D);
+  if ((visible_keys + BN - 1) / BN > kMaxTiles)
+    return set_error(TM_ERR_INVALID_ARGUMENT, "attention_plan: more than %d visible keys",
+                     kMaxTiles * BN);
+  const int tiles = static_cast<int>((visible_keys + BN - 1) / BN);
+  const Plan plan = make_plan(B, Lq, H, D, tiles, workspace_bytes);
+  const int64_t nq = (Lq + BM - 1) / BM;
+  int64_t n = 0;
+  if (plan.mode == 1)
+    n = static_cast<int64_t>(B) * H * nq * plan.kv_splits;
+  else if (plan.mode == 2)
+    n = static_cast<int64_t>(B) * (H * (nq / 2) + (H + 1) / 2);
+  else
+    n = static_cast<int64_t>(B) * H * (nq / 2 + (nq & 1));
+  *mode = plan.mode;
+  *kv_splits = plan.kv_splits;
+  *ctas = static_cast<int>(std::min<int64_t>(n, 0x7fffffff));
+  return TM_OK;
+}
+
 extern "C" int64_t tm_attention_partial_bytes(int B, int Lq, int H, int D, int splits) {
   using namespace tmb::attn;
   if (B < 1 || Lq < 1 || H < 1 || (D != 64 && D != 128) || splits < 1) return 0;
