@@ -157,6 +157,9 @@ def gelu_tanh_(x: Tensor) -> Tensor:
     return x
 
 
+_ADDMM_GELU = getattr(torch, "_addmm_activation", None)
+
+
 def feed_forward(ff, x: Tensor) -> Tensor:
     """``FeedForward`` (ltx_causal/transformer/compat.py:47-70): Linear ->
     tanh GELU -> Linear, both linears through cuBLAS.  With a bias the GELU
@@ -166,9 +169,11 @@ def feed_forward(ff, x: Tensor) -> Tensor:
     without one, ``tm_gelu_tanh`` in place."""
     proj = ff.net[0].proj
     x2 = x.reshape(-1, x.shape[-1])
-    if proj.bias is not None and x2.is_contiguous() and x2.shape[0] > 1 and \
-            proj.bias.dtype == x.dtype == proj.weight.dtype:
-        h = torch._addmm_activation(proj.bias, x2, proj.weight.t(), use_gelu=True)
+    # torch._addmm_activation is torch's own (private) entry to the epilogue;
+    # a torch without it takes the unfused path
+    if _ADDMM_GELU is not None and proj.bias is not None and x2.is_contiguous() and \
+            x2.shape[0] > 1 and proj.bias.dtype == x.dtype == proj.weight.dtype:
+        h = _ADDMM_GELU(proj.bias, x2, proj.weight.t(), use_gelu=True)
         h = h.view(*x.shape[:-1], h.shape[-1])
     else:
         h = F.linear(x, proj.weight, proj.bias)
