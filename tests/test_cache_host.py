@@ -190,3 +190,19 @@ def test_retention_slices_a_per_rank_v2a_cache_by_its_share():
     bad = LayerKVCache(video_self_k=vk, video_self_v=vv, v2a_k=ck, v2a_v=cv)
     with pytest.raises(ValueError):
         C.retain_streaming_context(C.attach_segments(KVCache(layers=[bad]), segs))
+
+
+def test_stream_block_geometry_follows_compute_av_blocks():
+    """The streaming runner's per-block geometry (video frames, audio tokens,
+    first video frame, first audio token) is the reference's 4-3-3-3 block
+    layout (compute_av_blocks with a first block of 4 frames) for the 181
+    latent frames of the 60 s stream."""
+    from oracle import ltx_oracle as O
+    from taomate_b200.model import StreamConfig
+    from taomate_b200.stream import block_geometry
+    cfg = StreamConfig(layers=1)
+    blocks = O.compute_av_blocks(181, 3, 4)
+    assert len(blocks) == 60  # 12 segments x 5 blocks: 4 + 59 x 3 frames
+    for k, (b, vs, ve, as_, ae) in enumerate(blocks):
+        assert b == k
+        assert block_geometry(k, cfg) == (ve - vs, ae - as_, vs, as_)
