@@ -37,13 +37,17 @@ typedef enum {
 
 enum { TM_DTYPE_BF16 = 0, TM_DTYPE_F32 = 1 };
 
-/* Version of this ABI (incremented on any signature change). */
+/* Version of this ABI (incremented on any signature change).  No counterpart
+ * in the reference (library housekeeping). */
 TM_API int tm_abi_version(void);
 
-/* Message of the last failed call on this thread ("" if none). */
+/* Message of the last failed call on this thread ("" if none).
+ * No counterpart in the reference: the Python layer raises it as the
+ * reference's exception types. */
 TM_API const char* tm_last_error(void);
 
 /*
+ * No counterpart in the reference (its torch ops have no device-side waits).
  * Read and clear the device-side error flag of the current device.  Blocks
  * until all prior work on the device has finished.  *code_out receives 0 when
  * no kernel reported an error, 1 when an attention kernel's bounded pipeline
@@ -295,6 +299,7 @@ TM_API int tm_attention_fwd_ws(const void* q, int64_t q_batch_stride, int64_t q_
                      void* stream);
 
 /*
+ * No counterpart in the reference (torch SDPA allocates its own scratch).
  * Workspace bytes tm_attention_fwd_ws uses for these shapes on the current
  * device (0: no key-range split).  visible_keys = total rows of all spans.
  */
@@ -369,6 +374,8 @@ typedef struct {
 } tm_attention_ext;
 
 /*
+ * No counterpart in the reference (it moves the V2A keys, not partial
+ * results, between GPUs).
  * Bytes of one export of tm_attention_fwd_ext `parts` with `splits` key
  * ranges: [splits][B][Lq][H][D] fp32 normalised outputs, then, at the next
  * 256-byte boundary, [splits][B][Lq][H] float2 (max * log2 scale, sum).
@@ -376,6 +383,7 @@ typedef struct {
 TM_API int64_t tm_attention_partial_bytes(int B, int Lq, int H, int D, int splits);
 
 /*
+ * No counterpart in the reference (as for tm_attention_partial_bytes).
  * Key ranges for an export over `visible_keys` keys that keep every SM busy
  * (the kernel's own work-partition cost model), >= 1.
  */
@@ -406,6 +414,8 @@ TM_API int tm_attention_fwd_ext(const void* q, int64_t q_batch_stride, int64_t q
                      int D, float scale, const tm_attention_ext* ext, void* stream);
 
 /*
+ * No counterpart in the reference (it concatenates the cache instead,
+ * kv_cache.py:1486-1492).
  * The key-tile list the attention kernel walks for a span list: n_tiles pairs
  * (source << 30 | first row, valid rows), 64 keys per tile, in span order.
  * Validates the spans as tm_attention_fwd does.  Used to refresh the device

@@ -118,3 +118,18 @@ def test_product_path_refuses_cpu_tensors():
         tm.flash_attention(q, None, None, [], q, q, 8)
     with pytest.raises(RuntimeError):
         tm.causal_precompute_freqs_cis(torch.tensor([[1, 2, 3]]), 256, device="cpu")
+
+
+def test_every_entry_point_cites_the_reference_or_says_it_has_none():
+    """Each declaration in include/*.h is documented by the comment right
+    before it (or before its group) with the reference function it replaces
+    (file.py:line) or with the words "no counterpart" and the reason."""
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        with open(h) as fh:
+            txt = fh.read()
+        comments = [(m.end(), m.group(0)) for m in re.finditer(r"/\*.*?\*/", txt, re.S)]
+        for m in re.finditer(r"TM_API\s+[\w\s\*]+?\b(tm_\w+)\s*\(", txt):
+            before = [c for end, c in comments if end <= m.start()]
+            doc = before[-1] if before else ""
+            assert re.search(r"\.py:\d+", doc) or re.search(r"no\s+counterpart", doc, re.I), \
+                f"{m.group(1)}: no reference citation or 'no counterpart' note"
